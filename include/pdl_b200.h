@@ -1,0 +1,183 @@
+/*
+ * pdl_b200.h -- C ABI of the B200 (sm_100a) paged decode-attention operator.
+ *
+ * One query token per sequence attends over a paged KV cache:
+ *   q        bf16 [batch, num_heads, head_dim]          (innermost stride 1)
+ *   k_cache  bf16 [num_pages, 256, num_kv_heads, head_dim]  contiguous NHD pages
+ *   v_cache  bf16 same shape as k_cache
+ *   table    int32 [batch, table_width]   logical page j of row b -> physical page
+ *   lengths  int32 [batch]                live tokens of row b
+ * Logical token t of row b is read from page table[b][t / 256], slot t % 256,
+ * KV head h / (num_heads / num_kv_heads).  Table entries past
+ * ceil(lengths[b] / 256) are padding (may be -1) and are never read.
+ *
+ * All entry points take raw device pointers and sizes, enqueue work on the
+ * given stream, never allocate, never synchronise and never read device
+ * memory from the host, so they may be captured in a CUDA graph (warm up
+ * once per device/geometry before capture).  They return PDL_OK or a
+ * PdlStatus; no C++ exception crosses this boundary.
+ */
+#ifndef PDL_B200_H
+#define PDL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *pdl_stream_t; /* same handle as cudaStream_t */
+
+#define PDL_ABI_VERSION 1
+#define PDL_PAGE_SIZE 256
+
+typedef enum PdlStatus {
+  PDL_OK = 0,
+  PDL_ERR_NULL = 1,        /* a required pointer is NULL                      */
+  PDL_ERR_GEOMETRY = 2,    /* head_dim / page size / head grouping unsupported */
+  PDL_ERR_SHAPE = 3,       /* batch, table width, pages or strides invalid     */
+  PDL_ERR_WORKSPACE = 4,   /* split workspace missing or too small             */
+  PDL_ERR_SCALE = 5,       /* scale not finite (or not positive where needed)  */
+  PDL_ERR_ALIGNMENT = 6,   /* pointer or stride not aligned for vector access  */
+  PDL_ERR_SPLITS = 7,      /* split count / size inconsistent with capacity    */
+  PDL_ERR_CUDA = 8,        /* a CUDA runtime or driver call failed             */
+  PDL_ERR_DEVICE = 9,      /* no usable sm_100 device                          */
+  PDL_ERR_KERNEL = 10,     /* requested kernel variant cannot run this shape   */
+  PDL_ERR_TIMEOUT = 11     /* a bounded device-side wait gave up (see fault)   */
+} PdlStatus;
+
+/* Which partial protocol the split workspace uses. */
+typedef enum PdlProtocol {
+  /* Normalised partial [B,Hq,S,D] + LSE [B,Hq,S] (natural log, scaled
+   * scores); empty partitions store partial 0 and LSE -inf. */
+  PDL_PROTOCOL_LSE = 0,
+  /* Unnormalised maxima / denominators [B,Hq,S] and accumulators [B,Hq,S,D];
+   * maxima are in scaled-score units, empty partitions store -inf / 0 / 0. */
+  PDL_PROTOCOL_MLA = 1
+} PdlProtocol;
+
+/* Which partition kernel runs. AUTO picks the tensor-core kernel when a KV
+ * head serves >= 8 query heads and the CUDA-core kernel otherwise. */
+typedef enum PdlKernel {
+  PDL_KERNEL_AUTO = 0,
+  PDL_KERNEL_SIMT = 1, /* FP32 CUDA-core kernel, warp-shuffle reductions      */
+  PDL_KERNEL_MMA = 2   /* BF16 tensor-core kernel (mma.sync), FP32 softmax    */
+} PdlKernel;
+
+/* Optional behaviour bits for PdlDecodeArgs.flags (0 = reference behaviour). */
+typedef enum PdlFlags {
+  /* Do not store empty partitions; the merge then reads only the
+   * ceil(len / tokens_per_split) live partitions of each row. */
+  PDL_FLAG_SKIP_EMPTY = 1,
+  /* With splits == 1, pdl_paged_decode writes the output directly from the
+   * partition kernel and leaves the workspace untouched. */
+  PDL_FLAG_DIRECT_SINGLE = 2
+} PdlFlags;
+
+/* Geometry contract; mirrors DecodeSpec (reference src/paged_decode/spec.py:11-30). */
+typedef struct PdlSpec {
+  int32_t max_batch;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;        /* 64, 128 or 256 */
+  int32_t max_context_len;
+  int32_t page_size;       /* must be 256 */
+} PdlSpec;
+
+/* Static split-KV plan; mirrors SplitKVPlan (reference src/paged_decode/splitkv_plan.py:15-23). */
+typedef struct PdlPlan {
+  int32_t splits;
+  int32_t tile_tokens;
+  int32_t tokens_per_split;
+  int32_t table_capacity_tokens;
+  int32_t lse_lanes;
+  int32_t sm_count;
+  int32_t explicit_splits;  /* 1: policy "explicit", 0: "pinned_geometry" */
+} PdlPlan;
+
+/* Arguments of one decode launch.  Element strides, not bytes. */
+typedef struct PdlDecodeArgs {
+  const void *q;              /* bf16 [batch, num_heads, head_dim]            */
+  int64_t q_stride_batch;
+  int64_t q_stride_head;
+  const void *k_cache;        /* bf16 [num_pages, 256, num_kv_heads, head_dim] */
+  const void *v_cache;
+  int64_t num_pages;
+  const int32_t *block_table; /* [batch, table_width], row stride below       */
+  int64_t table_stride;
+  int32_t table_width;
+  const int32_t *lengths;     /* [batch]                                      */
+  int32_t batch;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float scale;                /* softmax scale applied to q.k                 */
+  int32_t tokens_per_split;   /* partition size; 0 = one partition per row   */
+  int32_t splits;             /* partitions per row held by the workspace     */
+  int32_t protocol;           /* PdlProtocol                                  */
+  int32_t kernel;             /* PdlKernel                                    */
+  int32_t flags;              /* PdlFlags bits                                */
+  void *out;                  /* bf16 [batch, num_heads, head_dim] contiguous */
+  float *partial;             /* LSE protocol: [batch, num_heads, splits, head_dim] */
+  float *lse;                 /*               [batch, num_heads, splits]          */
+  float *maxima;              /* MLA protocol: [batch, num_heads, splits]          */
+  float *denoms;              /*               [batch, num_heads, splits]          */
+  float *accums;              /*               [batch, num_heads, splits, head_dim] */
+} PdlDecodeArgs;
+
+/* Partition kernel: per (row, KV head, partition) online softmax over the
+ * partition's tokens for every query head of the group; writes the split
+ * workspace in args->protocol.  With tokens_per_split == 0 and splits == 1 it
+ * writes the normalised output to args->out directly and needs no workspace.
+ * Replaces _normalized_partition (reference src/paged_decode/matched_splitkv.py:52-98),
+ * _split (src/paged_decode/kernels.py:44-80), _tc_partition
+ * (src/paged_decode/tc_splitk.py:13-60), _base (src/paged_decode/kernels.py:10-41)
+ * and _tensorcore (src/paged_decode/experimental_precision.py:46-107). */
+int pdl_partition(const PdlDecodeArgs *args, pdl_stream_t stream);
+
+/* Merge kernel: combines args->splits partitions per (row, query head) into
+ * bf16 args->out.  LSE protocol replaces _lse_merge
+ * (reference src/paged_decode/matched_splitkv.py:101-127); MLA protocol replaces
+ * _merge (src/paged_decode/kernels.py:83-100). */
+int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream);
+
+/* Partition + merge (or the single-pass kernel when tokens_per_split == 0).
+ * Replaces the launch sequence of paged_decode (reference
+ * src/paged_decode/runtime.py:87-117), matched_decode
+ * (src/paged_decode/matched_splitkv.py:130-150) and tc_splitk_decode
+ * (src/paged_decode/tc_splitk.py:63-79). */
+int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream);
+
+/* Static plan for `spec` on `sm_count` SMs; num_splits 0 = heuristic.
+ * Replaces make_splitkv_plan (reference src/paged_decode/splitkv_plan.py:26-56). */
+int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,
+                     PdlPlan *plan);
+
+/* partitions = ceil(max_context_len/1024), table_width = ceil(max_context_len/256),
+ * split workspace bytes = max_batch*num_heads*partitions*(head_dim+2)*4.
+ * Replaces DecodeSpec.partitions / table_width / split_workspace_bytes
+ * (reference src/paged_decode/spec.py:32-42) and the checks of
+ * DecodeSpec.__post_init__ (spec.py:20-30). */
+int pdl_spec_geometry(const PdlSpec *spec, int32_t *partitions, int32_t *table_width,
+                      int64_t *split_workspace_bytes);
+
+/* Human-readable name of a PdlStatus. */
+const char *pdl_status_string(int status);
+
+/* What the last failing call on this host thread tried and why (the CUDA
+ * error string, or the CUresult of descriptor encoding); "" if none. */
+const char *pdl_last_error(void);
+
+/* PDL_ABI_VERSION of the loaded library. */
+int pdl_abi_version(void);
+
+/* Sticky device-side fault word of the current device (0 = none); a
+ * non-zero value records which bounded wait gave up.  Synchronises the
+ * device; for diagnostics only, never on a hot path. */
+int pdl_read_fault(uint32_t *fault, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PDL_B200_H */

@@ -1,0 +1,41 @@
+"""FP32 gather + dense softmax on the GPU (oracle only; TEST INFRASTRUCTURE).
+
+Restates the reference's Torch oracle (src/paged_decode/torch_reference.py:5-17)
+for inputs too large for the NumPy oracle: every live row is gathered by its
+block table, upcast to FP32 and attended densely -- an algorithm independent
+of the split-K kernels it checks.  Rows of length 0 give zeros.
+"""
+import torch
+
+
+def dense_reference(q, k, v, tables, lengths, scale=None):
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    out = torch.zeros_like(q, dtype=torch.float32)
+    group = q.shape[1] // k.shape[2]
+    for b, n in enumerate(lengths.cpu().tolist()):
+        if n == 0:
+            continue
+        t = torch.arange(n, device=q.device)
+        pages = tables[b, t // 256].long()
+        keys = k[pages, t % 256].float().repeat_interleave(group, dim=1)
+        vals = v[pages, t % 256].float().repeat_interleave(group, dim=1)
+        scores = torch.einsum("hd,nhd->hn", q[b].float(), keys) * scale
+        out[b] = torch.einsum("hn,nhd->hd", scores.softmax(-1), vals)
+    return out
+
+
+def dense_lse(q, k, v, tables, lengths, start, stop, scale=None):
+    """Natural-log LSE of the scaled scores over tokens [start, stop) of each row."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    lse = torch.full(q.shape[:2], float("-inf"), dtype=torch.float32, device=q.device)
+    group = q.shape[1] // k.shape[2]
+    for b, n in enumerate(lengths.cpu().tolist()):
+        hi = min(stop, n)
+        if hi <= start:
+            continue
+        t = torch.arange(start, hi, device=q.device)
+        pages = tables[b, t // 256].long()
+        keys = k[pages, t % 256].float().repeat_interleave(group, dim=1)
+        scores = torch.einsum("hd,nhd->hn", q[b].float(), keys) * scale
+        lse[b] = torch.logsumexp(scores, dim=-1)
+    return lse

@@ -1,0 +1,411 @@
+// pdl_capi.cu -- extern "C" entry points declared in include/pdl_b200.h.
+//
+// Host-side only: argument validation (status codes, no exceptions), the
+// static split-KV plan, TMA descriptor encoding for the paged K/V pools, the
+// per-device state (SM count, fault word) and the launch sequence.  Nothing
+// here allocates device memory, synchronises, or reads device memory, so every
+// launch entry point can be captured in a CUDA graph.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "pdl_b200.h"
+#include "pdl_internal.h"
+
+// Sticky per-device fault word written by bounded device-side waits.
+__device__ uint32_t g_pdl_fault_word;
+
+namespace pdl {
+namespace {
+
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+  uint32_t *fault = nullptr;  // device address of g_pdl_fault_word
+};
+
+DeviceState g_devices[kMaxDevices];
+std::mutex g_mutex;
+
+// Description of the last failure on this host thread (pdl_last_error).
+thread_local char g_last_error[256] = "";
+
+int fail(int status, const char *where, const char *detail) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, detail ? detail : "");
+  return status;
+}
+
+int cuda_fail(const char *where, cudaError_t e) {
+  return fail(PDL_ERR_CUDA, where, cudaGetErrorString(e));
+}
+
+int current_device_state(DeviceState **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PDL_ERR_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return PDL_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState &st = g_devices[dev];
+  if (!st.ready) {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return PDL_ERR_DEVICE;
+    if (major != 10) return PDL_ERR_DEVICE;  // built for sm_100a only
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return PDL_ERR_DEVICE;
+    void *addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_pdl_fault_word);
+    if (e != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(fault word)", e);
+    st.sm_count = sms;
+    st.fault = static_cast<uint32_t *>(addr);
+    st.ready = true;
+  }
+  *out = &st;
+  return PDL_OK;
+}
+
+// cuTensorMapEncodeTiled from the driver, fetched through the runtime so the
+// library does not link libcuda directly.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// View of a paged pool [pages, 256, Hkv, D] as a 4-D tensor (D, Hkv, 256,
+// pages) with boxes of (64 columns, 1 head, box_tokens slots, 1 page): one
+// box is one 128-byte column band of box_tokens consecutive slots of one KV
+// head inside one page, landed with the 128-byte swizzle.
+int encode_pool_map(CUtensorMap *map, const void *base, int64_t pages, int hkv, int dim,
+                    int box_tokens) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return fail(PDL_ERR_CUDA, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled");
+  const cuuint64_t dims[4] = {(cuuint64_t)dim, (cuuint64_t)hkv, 256u, (cuuint64_t)pages};
+  const cuuint64_t strides[3] = {(cuuint64_t)dim * 2, (cuuint64_t)hkv * dim * 2,
+                                 (cuuint64_t)256 * hkv * dim * 2};
+  const cuuint32_t box[4] = {64u, 1u, (cuuint32_t)box_tokens, 1u};
+  const cuuint32_t elem[4] = {1u, 1u, 1u, 1u};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims,
+                        strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char detail[96];
+    snprintf(detail, sizeof(detail), "CUresult %d", (int)r);
+    return fail(PDL_ERR_CUDA, "cuTensorMapEncodeTiled", detail);
+  }
+  return PDL_OK;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool valid_dim(int d) { return d == 64 || d == 128 || d == 256; }
+
+// Which partition kernel serves this launch.
+int choose_kernel(const PdlDecodeArgs &a) {
+  const int group = a.num_heads / a.num_kv_heads;
+  if (a.kernel == PDL_KERNEL_SIMT) return PDL_KERNEL_SIMT;
+  if (a.kernel == PDL_KERNEL_MMA) return PDL_KERNEL_MMA;
+  return group >= 8 ? PDL_KERNEL_MMA : PDL_KERNEL_SIMT;
+}
+
+// Checks shared by every launch entry point; mirrors the tensor contract of
+// the reference's _validate (src/paged_decode/runtime.py:46-84) on raw
+// pointers and sizes.
+int validate_common(const PdlDecodeArgs *a) {
+  if (a == nullptr) return PDL_ERR_NULL;
+  if (!valid_dim(a->head_dim)) return PDL_ERR_GEOMETRY;
+  if (a->num_heads <= 0 || a->num_kv_heads <= 0 || a->num_heads % a->num_kv_heads)
+    return PDL_ERR_GEOMETRY;
+  if (a->batch <= 0 || a->batch > 65535) return PDL_ERR_SHAPE;
+  if (!std::isfinite(a->scale)) return PDL_ERR_SCALE;
+  if (a->splits <= 0 || a->tokens_per_split < 0) return PDL_ERR_SPLITS;
+  if (a->tokens_per_split == 0 && a->splits != 1) return PDL_ERR_SPLITS;
+  if (a->protocol != PDL_PROTOCOL_LSE && a->protocol != PDL_PROTOCOL_MLA) return PDL_ERR_SHAPE;
+  return PDL_OK;
+}
+
+int validate_partition_inputs(const PdlDecodeArgs *a) {
+  if (!a->q || !a->k_cache || !a->v_cache || !a->block_table || !a->lengths) return PDL_ERR_NULL;
+  if (a->num_pages <= 0 || a->num_pages > INT32_MAX) return PDL_ERR_SHAPE;
+  if (a->table_width <= 0 || a->table_stride < a->table_width) return PDL_ERR_SHAPE;
+  if (a->q_stride_head < a->head_dim || a->q_stride_batch < 1) return PDL_ERR_SHAPE;
+  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)) return PDL_ERR_ALIGNMENT;
+  if (!aligned(a->q, 2)) return PDL_ERR_ALIGNMENT;
+  if (a->tokens_per_split > 0) {
+    // Every token the table can address must belong to some partition.
+    const int64_t covered = (int64_t)a->splits * a->tokens_per_split;
+    if (covered < (int64_t)a->table_width * PDL_PAGE_SIZE) return PDL_ERR_SPLITS;
+  }
+  return PDL_OK;
+}
+
+int validate_workspace(const PdlDecodeArgs *a) {
+  if (a->protocol == PDL_PROTOCOL_LSE) {
+    if (!a->partial || !a->lse) return PDL_ERR_WORKSPACE;
+    if (!aligned(a->partial, 16)) return PDL_ERR_ALIGNMENT;
+  } else {
+    if (!a->maxima || !a->denoms || !a->accums) return PDL_ERR_WORKSPACE;
+    if (!aligned(a->accums, 16)) return PDL_ERR_ALIGNMENT;
+  }
+  return PDL_OK;
+}
+
+int validate_out(const PdlDecodeArgs *a) {
+  if (!a->out) return PDL_ERR_NULL;
+  if (!aligned(a->out, 16)) return PDL_ERR_ALIGNMENT;
+  return PDL_OK;
+}
+
+int status_from_cuda(cudaError_t e, const char *where) {
+  return e == cudaSuccess ? PDL_OK : cuda_fail(where, e);
+}
+
+// Launch the partition kernel in `mode` (MODE_LSE / MODE_MLA / MODE_DIRECT).
+int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
+  DeviceState *dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != PDL_OK) return st;
+  const int which = choose_kernel(*a);
+  const int group = a->num_heads / a->num_kv_heads;
+  int per_cta = 0, box = 0;
+  if (which == PDL_KERNEL_SIMT) {
+    per_cta = simt_heads_per_cta(group);
+    box = simt_tile_tokens(a->head_dim);
+  } else {
+    per_cta = mma_heads_per_cta(group, a->head_dim);
+    box = mma_tile_tokens(a->head_dim);
+    if (per_cta <= 0) return PDL_ERR_KERNEL;
+  }
+  const int nsub = (group + per_cta - 1) / per_cta;
+  const int64_t items = (int64_t)a->splits * a->num_kv_heads * nsub * a->batch;
+  if (items > INT32_MAX) return PDL_ERR_SHAPE;
+
+  CUtensorMap kmap, vmap;
+  st = encode_pool_map(&kmap, a->k_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
+  if (st != PDL_OK) return st;
+  st = encode_pool_map(&vmap, a->v_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
+  if (st != PDL_OK) return st;
+
+  KernelLaunch L;
+  std::memset(&L, 0, sizeof(L));
+  L.k_map = &kmap;
+  L.v_map = &vmap;
+  L.head_dim = a->head_dim;
+  L.group_per_cta = per_cta;
+  L.sm_count = dev->sm_count;
+  PartitionParams &p = L.params;
+  p.q = static_cast<const __nv_bfloat16 *>(a->q);
+  p.q_stride_batch = a->q_stride_batch;
+  p.q_stride_head = a->q_stride_head;
+  p.table = a->block_table;
+  p.table_stride = a->table_stride;
+  p.table_width = a->table_width;
+  p.lengths = a->lengths;
+  p.batch = a->batch;
+  p.num_heads = a->num_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.group = group;
+  p.nsub = nsub;
+  p.tokens_per_split = a->tokens_per_split > 0 ? a->tokens_per_split : (1 << 30);
+  p.splits = a->splits;
+  p.n_items = (int32_t)items;
+  p.log2_scale = a->scale * 1.4426950408889634f;
+  p.mode = mode;
+  p.q_vec16 = aligned(a->q, 16) && (a->q_stride_batch % 8 == 0) && (a->q_stride_head % 8 == 0);
+  p.write_empty = (a->flags & PDL_FLAG_SKIP_EMPTY) ? 0 : 1;
+  p.out = static_cast<__nv_bfloat16 *>(a->out);
+  p.partial = a->partial;
+  p.lse = a->lse;
+  p.maxima = a->maxima;
+  p.denoms = a->denoms;
+  p.accums = a->accums;
+  p.fault = dev->fault;
+  const cudaError_t e = which == PDL_KERNEL_SIMT ? launch_partition_simt(L, stream)
+                                                 : launch_partition_mma(L, stream);
+  return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
+}
+
+int run_merge(const PdlDecodeArgs *a, cudaStream_t stream) {
+  MergeParams m;
+  std::memset(&m, 0, sizeof(m));
+  m.partial = a->partial;
+  m.lse = a->lse;
+  m.maxima = a->maxima;
+  m.denoms = a->denoms;
+  m.accums = a->accums;
+  m.out = static_cast<__nv_bfloat16 *>(a->out);
+  m.lengths = (a->flags & PDL_FLAG_SKIP_EMPTY) ? a->lengths : nullptr;
+  m.num_heads = a->num_heads;
+  m.tokens_per_split = a->tokens_per_split > 0 ? a->tokens_per_split : (1 << 30);
+  m.rows = a->batch * a->num_heads;
+  m.splits = a->splits;
+  m.protocol = a->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA;
+  return status_from_cuda(launch_merge(m, a->head_dim, stream), "merge");
+}
+
+float to_f32(double x) { return static_cast<float>(x); }
+
+}  // namespace
+}  // namespace pdl
+
+using namespace pdl;
+
+extern "C" int pdl_abi_version(void) { return PDL_ABI_VERSION; }
+
+extern "C" const char *pdl_last_error(void) { return g_last_error; }
+
+extern "C" const char *pdl_status_string(int status) {
+  switch (status) {
+    case PDL_OK: return "ok";
+    case PDL_ERR_NULL: return "null pointer";
+    case PDL_ERR_GEOMETRY: return "unsupported geometry";
+    case PDL_ERR_SHAPE: return "invalid shape or stride";
+    case PDL_ERR_WORKSPACE: return "invalid or missing preallocated split-K workspace";
+    case PDL_ERR_SCALE: return "invalid scale";
+    case PDL_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case PDL_ERR_SPLITS: return "invalid split configuration";
+    case PDL_ERR_CUDA: return "CUDA call failed";
+    case PDL_ERR_DEVICE: return "no usable sm_100 device";
+    case PDL_ERR_KERNEL: return "kernel variant unavailable for this shape";
+    case PDL_ERR_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int pdl_spec_geometry(const PdlSpec *spec, int32_t *partitions, int32_t *table_width,
+                                 int64_t *split_workspace_bytes) {
+  if (!spec) return PDL_ERR_NULL;
+  if (spec->max_batch <= 0 || spec->num_heads <= 0 || spec->num_kv_heads <= 0 ||
+      spec->max_context_len <= 0)
+    return PDL_ERR_SHAPE;
+  if (!valid_dim(spec->head_dim) || spec->page_size != PDL_PAGE_SIZE ||
+      spec->num_heads % spec->num_kv_heads)
+    return PDL_ERR_GEOMETRY;
+  const int64_t parts = ((int64_t)spec->max_context_len + 1023) / 1024;
+  const int64_t width = ((int64_t)spec->max_context_len + PDL_PAGE_SIZE - 1) / PDL_PAGE_SIZE;
+  if (partitions) *partitions = (int32_t)parts;
+  if (table_width) *table_width = (int32_t)width;
+  if (split_workspace_bytes)
+    *split_workspace_bytes =
+        (int64_t)spec->max_batch * spec->num_heads * parts * (spec->head_dim + 2) * 4;
+  return PDL_OK;
+}
+
+// Static plan: same integer and float32 steps as the reference heuristic
+// (src/paged_decode/splitkv_plan.py:26-56).  Python floats are doubles there;
+// every _f32() rounding is a cast to float here.
+extern "C" int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,
+                                PdlPlan *plan) {
+  if (!spec || !plan) return PDL_ERR_NULL;
+  int st = pdl_spec_geometry(spec, nullptr, nullptr, nullptr);
+  if (st != PDL_OK) return st;
+  if (sm_count < 1) return PDL_ERR_SHAPE;
+  if (num_splits < 0 || num_splits > 128) return PDL_ERR_SPLITS;
+  if (spec->num_heads / spec->num_kv_heads > 16) return PDL_ERR_GEOMETRY;
+  const int tile = spec->head_dim == 64 ? 256 : (spec->head_dim == 128 ? 128 : 64);
+  const int64_t capacity = ((int64_t)spec->max_context_len + 255) / 256 * 256;
+  const int64_t blocks = (capacity + tile - 1) / tile;
+  int64_t splits = num_splits;
+  if (splits == 0) {
+    const int64_t work = (int64_t)spec->max_batch * spec->num_kv_heads;
+    const int64_t virt = (int64_t)sm_count * 2;
+    const float threshold = to_f32((double)to_f32(0.8) * (double)virt);
+    if ((double)work >= (double)threshold) {
+      splits = 1;
+    } else {
+      const int64_t maximum = std::min<int64_t>(std::min<int64_t>(128, virt), blocks);
+      float eff[129];
+      bool ok[129];
+      float best = 0.f;
+      for (int64_t n = 1; n <= maximum; ++n) {
+        ok[n] = n == 1 || (blocks + n - 1) / n != (blocks + n - 2) / (n - 1);
+        if (!ok[n]) continue;
+        const float waves = to_f32((double)to_f32((double)(work * n)) / (double)virt);
+        eff[n] = to_f32((double)waves / std::ceil((double)waves));
+        best = std::max(best, eff[n]);
+      }
+      splits = 1;
+      for (int64_t n = 1; n <= maximum; ++n) {
+        if (ok[n] && (double)eff[n] >= 0.85 * (double)best) {
+          splits = n;
+          break;
+        }
+      }
+    }
+  }
+  int64_t padded = 1;
+  while (padded < splits) padded <<= 1;
+  const int64_t merge_rows = spec->head_dim % 128 == 0 ? 4 : 8;
+  plan->splits = (int32_t)splits;
+  plan->tile_tokens = tile;
+  plan->tokens_per_split = (int32_t)((blocks + splits - 1) / splits * tile);
+  plan->table_capacity_tokens = (int32_t)capacity;
+  plan->lse_lanes = (int32_t)std::min<int64_t>(padded, 128 / merge_rows);
+  plan->sm_count = sm_count;
+  plan->explicit_splits = num_splits ? 1 : 0;
+  return PDL_OK;
+}
+
+extern "C" int pdl_partition(const PdlDecodeArgs *args, pdl_stream_t stream) {
+  int st = validate_common(args);
+  if (st == PDL_OK) st = validate_partition_inputs(args);
+  if (st != PDL_OK) return st;
+  const bool direct = args->tokens_per_split == 0;
+  st = direct ? validate_out(args) : validate_workspace(args);
+  if (st != PDL_OK) return st;
+  const int mode = direct ? MODE_DIRECT
+                          : (args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA);
+  return run_partition(args, mode, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream) {
+  int st = validate_common(args);
+  if (st != PDL_OK) return st;
+  if ((args->flags & PDL_FLAG_SKIP_EMPTY) && !args->lengths) return PDL_ERR_NULL;
+  st = validate_workspace(args);
+  if (st == PDL_OK) st = validate_out(args);
+  if (st != PDL_OK) return st;
+  return run_merge(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) {
+  int st = validate_common(args);
+  if (st == PDL_OK) st = validate_partition_inputs(args);
+  if (st == PDL_OK) st = validate_out(args);
+  if (st != PDL_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool direct = args->tokens_per_split == 0 ||
+                      (args->splits == 1 && (args->flags & PDL_FLAG_DIRECT_SINGLE));
+  if (direct) return run_partition(args, MODE_DIRECT, s);
+  st = validate_workspace(args);
+  if (st != PDL_OK) return st;
+  st = run_partition(args, args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA, s);
+  if (st != PDL_OK) return st;
+  return run_merge(args, s);
+}
+
+extern "C" int pdl_read_fault(uint32_t *fault, int clear) {
+  if (!fault) return PDL_ERR_NULL;
+  DeviceState *dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != PDL_OK) return st;
+  if (cudaDeviceSynchronize() != cudaSuccess) return PDL_ERR_CUDA;
+  if (cudaMemcpy(fault, dev->fault, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return PDL_ERR_CUDA;
+  if (clear && cudaMemset(dev->fault, 0, sizeof(uint32_t)) != cudaSuccess) return PDL_ERR_CUDA;
+  return PDL_OK;
+}

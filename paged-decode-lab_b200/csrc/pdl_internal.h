@@ -1,0 +1,89 @@
+// pdl_internal.h -- parameter blocks shared by the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pdl {
+
+constexpr int kMaxDevices = 64;
+
+// What the partition kernel stores per (row, query head, partition).
+enum OutMode : int {
+  MODE_LSE = 0,     // normalised partial + LSE
+  MODE_MLA = 1,     // unnormalised maxima / denominators / accumulators
+  MODE_DIRECT = 2,  // one partition per row: normalised BF16 output
+};
+
+// Work item = (row b, KV head, head sub-group, partition); items are
+// enumerated partition-fastest and handed to persistent CTAs round-robin.
+struct PartitionParams {
+  const __nv_bfloat16 *q;
+  int64_t q_stride_batch;   // elements
+  int64_t q_stride_head;    // elements
+  const int32_t *table;
+  int64_t table_stride;     // elements
+  int32_t table_width;      // live tokens are clamped to table_width * 256
+  const int32_t *lengths;
+  int32_t batch;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t group;            // num_heads / num_kv_heads
+  int32_t nsub;             // head sub-groups per KV head
+  int32_t tokens_per_split; // > 0
+  int32_t splits;
+  int32_t n_items;          // splits * num_kv_heads * nsub * batch
+  float log2_scale;         // scale * log2(e)
+  int32_t mode;             // OutMode
+  int32_t q_vec16;          // q rows 16-byte aligned (vector loads)
+  int32_t write_empty;      // store -inf/0 for empty partitions
+  __nv_bfloat16 *out;
+  float *partial;
+  float *lse;
+  float *maxima;
+  float *denoms;
+  float *accums;
+  uint32_t *fault;          // per-device fault word
+};
+
+struct MergeParams {
+  const float *partial;     // LSE protocol
+  const float *lse;
+  const float *maxima;      // MLA protocol
+  const float *denoms;
+  const float *accums;
+  __nv_bfloat16 *out;
+  const int32_t *lengths;   // optional: bound the partitions read per row
+  int32_t num_heads;
+  int32_t tokens_per_split;
+  int32_t rows;             // batch * num_heads
+  int32_t splits;
+  int32_t protocol;         // MODE_LSE or MODE_MLA
+};
+
+struct KernelLaunch {
+  const CUtensorMap *k_map;
+  const CUtensorMap *v_map;
+  PartitionParams params;
+  int head_dim;
+  int group_per_cta;        // query heads handled by one CTA
+  int sm_count;
+};
+
+// Launchers (return a cudaError_t).  Each configures its kernel's shared
+// memory on first use and sizes a persistent grid from the occupancy query.
+cudaError_t launch_partition_simt(const KernelLaunch &launch, cudaStream_t stream);
+cudaError_t launch_partition_mma(const KernelLaunch &launch, cudaStream_t stream);
+cudaError_t launch_merge(const MergeParams &params, int head_dim, cudaStream_t stream);
+
+// Query heads per CTA each kernel supports for a given group size.
+int simt_heads_per_cta(int group);
+int mma_heads_per_cta(int group, int head_dim);
+
+// Tokens per pipeline stage (TMA box height) of each kernel for a head dim.
+int simt_tile_tokens(int head_dim);
+int mma_tile_tokens(int head_dim);
+
+}  // namespace pdl

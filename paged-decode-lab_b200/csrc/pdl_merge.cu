@@ -1,0 +1,121 @@
+// pdl_merge.cu -- stable merge of split-K partitions into the BF16 output.
+//
+// One warp per (row, query head); lane l owns D/32 contiguous FP32 columns,
+// so each partition row is read with one coalesced vector load per lane.
+//
+// LSE protocol (reference src/paged_decode/matched_splitkv.py:101-127):
+//   M = max_p lse_p (an all -inf row uses 0); total = sum_p exp(lse_p - M);
+//   logsum = ln(total) + M, or +inf when total = 0;
+//   out = sum_p exp(lse_p - logsum) * partial_p.
+// MLA protocol (reference src/paged_decode/kernels.py:83-100):
+//   M = max_p m_p (-inf -> 0); f_p = exp(m_p - M);
+//   out = sum_p f_p * acc_p / (sum_p f_p * l_p, or 1 when that is 0).
+// When the caller passes `lengths`, only the ceil(len / tokens_per_split)
+// live partitions of a row are read (the others hold no tokens and their
+// weights are exactly 0), so empty partitions need not be stored at all.
+#include "pdl_device.cuh"
+
+namespace pdl {
+namespace {
+
+constexpr int MERGE_WARPS = 4;
+
+template <int E>
+__device__ __forceinline__ void load_cols(const float *src, float (&v)[E]) {
+  if constexpr (E == 2) {
+    const float2 a = *reinterpret_cast<const float2 *>(src);
+    v[0] = a.x; v[1] = a.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; i += 4) {
+      const float4 a = *reinterpret_cast<const float4 *>(src + i);
+      v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL_MASK, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);
+  return v;
+}
+
+template <int D>
+__global__ void __launch_bounds__(32 * MERGE_WARPS)
+    merge_kernel(const MergeParams p) {
+  constexpr int E = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  int live = p.splits;
+  if (p.lengths != nullptr) {
+    const int len = __ldg(p.lengths + row / p.num_heads);
+    live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+  }
+  const int64_t base = (int64_t)row * p.splits;
+  const float *weights_src = p.protocol == MODE_LSE ? p.lse : p.maxima;
+
+  float mx = -INFINITY;
+  for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldg(weights_src + base + s));
+  mx = warp_max(mx);
+  if (mx == -INFINITY) mx = 0.f;
+
+  float shift = mx;  // exponent subtracted from every weight
+  float scale = 1.f; // final multiplier
+  if (p.protocol == MODE_LSE) {
+    float tot = 0.f;
+    for (int s = lane; s < live; s += 32) tot += expf(__ldg(p.lse + base + s) - mx);
+    tot = warp_sum(tot);
+    shift = tot > 0.f ? logf(tot) + mx : INFINITY;
+  } else {
+    float tot = 0.f;
+    for (int s = lane; s < live; s += 32)
+      tot += __ldg(p.denoms + base + s) * expf(__ldg(p.maxima + base + s) - mx);
+    tot = warp_sum(tot);
+    scale = 1.f / (tot > 0.f ? tot : 1.f);
+  }
+
+  const float *rows_src = p.protocol == MODE_LSE ? p.partial : p.accums;
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  for (int s0 = 0; s0 < live; s0 += 32) {
+    const float wl = (s0 + lane < live) ? expf(__ldg(weights_src + base + s0 + lane) - shift) : 0.f;
+    const int n = min(32, live - s0);
+    for (int k = 0; k < n; ++k) {
+      const float wk = __shfl_sync(FULL_MASK, wl, k);
+      float v[E];
+      load_cols<E>(rows_src + (base + s0 + k) * D + lane * E, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[e], acc[e]);
+    }
+  }
+  __nv_bfloat16 *dst = p.out + (int64_t)row * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    *reinterpret_cast<__nv_bfloat162 *>(dst + e) =
+        __floats2bfloat162_rn(acc[e] * scale, acc[e + 1] * scale);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_merge(const MergeParams &params, int head_dim, cudaStream_t stream) {
+  const int grid = (params.rows + MERGE_WARPS - 1) / MERGE_WARPS;
+  if (grid <= 0) return cudaSuccess;
+  switch (head_dim) {
+    case 64: merge_kernel<64><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
+    case 128: merge_kernel<128><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
+    case 256: merge_kernel<256><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pdl

@@ -1,0 +1,216 @@
+// pdl_pipeline.cuh -- pieces shared by the partition kernels: work-item
+// decoding, the TMA producer warp, stores for empty partitions, and the
+// merge of the consumer warps' softmax states into the stored outputs.
+#pragma once
+
+#include "pdl_device.cuh"
+
+namespace pdl {
+
+struct Item {
+  int b, kvh, sub, split;
+};
+
+// item = ((b * num_kv_heads + kvh) * nsub + sub) * splits + split
+__device__ __forceinline__ Item decode_item(const PartitionParams &p, int item) {
+  Item it;
+  it.split = item % p.splits;
+  const int rest = item / p.splits;
+  const int per_row = p.num_kv_heads * p.nsub;
+  it.b = rest / per_row;
+  const int r = rest % per_row;
+  it.kvh = r / p.nsub;
+  it.sub = r % p.nsub;
+  return it;
+}
+
+// Token range [start, stop) of an item; empty when start >= stop.  Lengths
+// beyond the table capacity are clamped to it, so no table entry past the
+// row's width is ever read.
+struct Range {
+  int start, stop;
+};
+
+__device__ __forceinline__ Range item_range(const PartitionParams &p, const Item &w) {
+  const int len = min(__ldg(p.lengths + w.b), p.table_width * 256);
+  const int64_t start = (int64_t)w.split * p.tokens_per_split;
+  const int64_t stop = min((int64_t)len, start + p.tokens_per_split);
+  Range r;
+  r.start = start >= stop ? 0 : (int)start;
+  r.stop = start >= stop ? 0 : (int)stop;
+  return r;
+}
+
+// Stores for a partition with no live tokens: partial 0 / LSE -inf,
+// (m, l, acc) = (-inf, 0, 0), or a zero output row.
+template <int D>
+__device__ void store_empty(const PartitionParams &p, int b, int h0, int rows, int split,
+                            int tid, int nthreads) {
+  for (int e = tid; e < rows * D; e += nthreads) {
+    const int g = e / D, d = e % D;
+    const int64_t row = (int64_t)b * p.num_heads + h0 + g;
+    const int64_t idx = row * p.splits + split;
+    if (p.mode == MODE_LSE) {
+      p.partial[idx * D + d] = 0.f;
+      if (d == 0) p.lse[idx] = -INFINITY;
+    } else if (p.mode == MODE_MLA) {
+      p.accums[idx * D + d] = 0.f;
+      if (d == 0) {
+        p.maxima[idx] = -INFINITY;
+        p.denoms[idx] = 0.f;
+      }
+    } else {
+      p.out[row * D + d] = __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
+// Producer warp: for every item of this CTA, in the consumers' order, read
+// the live block-table entries (32 per load, one per lane, never past
+// ceil(stop/256)) and issue one T-token tile of K and V per stage as
+// D/64 TMA boxes each.  T divides 256, so a tile never spans two pages.
+template <int D, int T, int NS>
+__device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
+                             const PartitionParams &p, uint8_t *kbuf, uint8_t *vbuf,
+                             uint64_t *full, uint64_t *empty, volatile int *abort_flag,
+                             int lane) {
+  constexpr int SUBTILES = D / 64;
+  constexpr int SUB_BYTES = T * 128;
+  constexpr int TILE_BYTES = T * D * 2;
+  const uint64_t policy = l2_evict_first_policy();
+  if (lane == 0) {
+    prefetch_tensormap(k_map);
+    prefetch_tensormap(v_map);
+  }
+  uint32_t it = 0;
+  bool ok = true;
+  for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+    const Item w = decode_item(p, item);
+    const Range r = item_range(p, w);
+    if (r.start >= r.stop) continue;
+    const int t0 = r.start / T * T;
+    const int ntiles = (r.stop - t0 + T - 1) / T;
+    const int live_pages = (r.stop + 255) >> 8;
+    const int32_t *trow = p.table + (int64_t)w.b * p.table_stride;
+    int base = -64, my_page = 0;
+    for (int i = 0; i < ntiles; ++i, ++it) {
+      const int tok = t0 + i * T;
+      const int pg = tok >> 8;
+      if (pg >= base + 32) {
+        base = pg;
+        my_page = (pg + lane < live_pages) ? __ldg(trow + pg + lane) : 0;
+      }
+      const int page = __shfl_sync(FULL_MASK, my_page, pg - base);
+      if (lane == 0) {
+        const int s = it % NS;
+        if (it >= NS && !pipeline_wait(&empty[s], ((it / NS) & 1) ^ 1, p.fault,
+                                       FAULT_PRODUCER_EMPTY_WAIT, abort_flag)) {
+          ok = false;
+        } else {
+          mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+#pragma unroll
+          for (int st = 0; st < SUBTILES; ++st) {
+            tma_load_4d(kbuf + s * TILE_BYTES + st * SUB_BYTES, k_map, st * 64, w.kvh, tok & 255,
+                        page, &full[s], policy);
+            tma_load_4d(vbuf + s * TILE_BYTES + st * SUB_BYTES, v_map, st * 64, w.kvh, tok & 255,
+                        page, &full[s], policy);
+          }
+        }
+      }
+      ok = __shfl_sync(FULL_MASK, ok, 0);
+      if (!ok) break;
+    }
+  }
+  if (!ok && lane == 0) {
+    // Let the copies already issued land before the CTA exits.
+    const uint32_t first = it > NS ? it - NS : 0;
+    for (uint32_t k = first; k < it; ++k)
+      mbar_wait_bounded(&full[k % NS], (k / NS) & 1, p.fault, FAULT_DRAIN_WAIT);
+  }
+}
+
+// Merge NC per-warp softmax states of one item and store the outputs.
+//   comb_acc [NC][GC][D]  unnormalised accumulators (relative to each warp's max)
+//   comb_ml  [NC][2][GC]  per-warp running max (base-2 scaled units) and sum
+// M = max_w m_w; f_w = 2^(m_w - M); L = sum f_w l_w; O = sum f_w acc_w.
+// Stores O/L + LSE (natural log), (M ln2, L, O), or BF16 O/L.
+template <int D, int GC, int NC>
+__device__ void combine_and_store(const PartitionParams &p, const Item &w, int h0, int rows,
+                                  const float *comb_acc, const float *comb_ml, int tid) {
+  for (int e = tid * 4; e < rows * D; e += NC * 32 * 4) {
+    const int g = e / D, d = e % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int wi = 0; wi < NC; ++wi) mx = fmaxf(mx, comb_ml[wi * 2 * GC + g]);
+    float den = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int wi = 0; wi < NC; ++wi) {
+      const float mw = comb_ml[wi * 2 * GC + g];
+      const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+      den += f * comb_ml[wi * 2 * GC + GC + g];
+      const float4 a = *reinterpret_cast<const float4 *>(comb_acc + (wi * GC + g) * D + d);
+      o.x += f * a.x;
+      o.y += f * a.y;
+      o.z += f * a.z;
+      o.w += f * a.w;
+    }
+    const int64_t row = (int64_t)w.b * p.num_heads + h0 + g;
+    const int64_t idx = row * p.splits + w.split;
+    if (p.mode == MODE_MLA) {
+      *reinterpret_cast<float4 *>(p.accums + idx * D + d) = o;
+      if (d == 0) {
+        p.maxima[idx] = mx * LN2;
+        p.denoms[idx] = den;
+      }
+    } else {
+      const float inv = 1.f / den;
+      o.x *= inv;
+      o.y *= inv;
+      o.z *= inv;
+      o.w *= inv;
+      if (p.mode == MODE_LSE) {
+        *reinterpret_cast<float4 *>(p.partial + idx * D + d) = o;
+        if (d == 0) p.lse[idx] = (mx + log2f(den)) * LN2;
+      } else {
+        __nv_bfloat162 lo2 = __floats2bfloat162_rn(o.x, o.y);
+        __nv_bfloat162 hi2 = __floats2bfloat162_rn(o.z, o.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t *>(&lo2);
+        packed.y = *reinterpret_cast<uint32_t *>(&hi2);
+        *reinterpret_cast<uint2 *>(p.out + row * D + d) = packed;
+      }
+    }
+  }
+}
+
+// Dynamic shared memory one CTA may use so that two CTAs share an SM
+// (228 KB per SM, 1 KB reserved per CTA).
+constexpr int kTwoCtaSmemBytes = 233472 / 2 - 1024;
+
+// The swizzle arithmetic assumes the dynamic shared-memory base is 1024-byte
+// aligned (it is when a kernel has no static shared memory).  If it ever is
+// not, the CTA records FAULT_SMEM_ALIGN and returns without touching memory.
+__device__ __forceinline__ bool smem_base_aligned(const void *smem, uint32_t *fault) {
+  if ((smem_u32(smem) & 1023u) == 0) return true;
+  if (threadIdx.x == 0 && fault) atomicOr(fault, FAULT_SMEM_ALIGN);
+  return false;
+}
+
+// Shared-memory plan of a partition kernel: K ring | V ring | per-warp
+// accumulators [NC][GC][D] | per-warp (m, l) [NC][2][GC] | mbarriers | flag.
+template <int D, int T, int NS, int NC, int GC>
+struct PartitionSmem {
+  static constexpr int TILE_BYTES = T * D * 2;
+  static constexpr int KV_BYTES = 2 * NS * TILE_BYTES;
+  static constexpr int ACC_FLOATS = NC * GC * D;
+  static constexpr int ML_FLOATS = NC * 2 * GC;
+  static constexpr int BAR_OFFSET = KV_BYTES + (ACC_FLOATS + ML_FLOATS) * 4;
+  static constexpr int BYTES = BAR_OFFSET + 2 * NS * 8 + 16;
+  static_assert(TILE_BYTES % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+  static_assert((T * 128) % 1024 == 0, "swizzled sub-tiles need 1024-byte alignment");
+  static_assert((GC * D * 4) % 16 == 0, "per-warp accumulators are accessed as float4");
+  static_assert(BAR_OFFSET % 8 == 0, "mbarriers need 8-byte alignment");
+};
+
+}  // namespace pdl

@@ -1,0 +1,109 @@
+"""ctypes binding of the C ABI in ``include/pdl_b200.h`` (``libpdl_b200.so``).
+
+The shared library is built in-tree by ``csrc/build.py``.  There is no
+fallback: if it is missing or stale, every op raises instead of computing
+anything another way.
+"""
+import ctypes
+from pathlib import Path
+
+LIBRARY = Path(__file__).with_name("libpdl_b200.so")
+ABI_VERSION = 1
+
+PDL_OK = 0
+STATUS_NAMES = {
+    0: "PDL_OK", 1: "PDL_ERR_NULL", 2: "PDL_ERR_GEOMETRY", 3: "PDL_ERR_SHAPE",
+    4: "PDL_ERR_WORKSPACE", 5: "PDL_ERR_SCALE", 6: "PDL_ERR_ALIGNMENT", 7: "PDL_ERR_SPLITS",
+    8: "PDL_ERR_CUDA", 9: "PDL_ERR_DEVICE", 10: "PDL_ERR_KERNEL", 11: "PDL_ERR_TIMEOUT",
+}
+PROTOCOL_LSE, PROTOCOL_MLA = 0, 1
+KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
+FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE = 1, 2
+
+# Every extern "C" symbol declared in include/pdl_b200.h.
+SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_paged_decode", "pdl_splitkv_plan",
+           "pdl_spec_geometry", "pdl_status_string", "pdl_last_error", "pdl_abi_version",
+           "pdl_read_fault")
+
+_i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+
+class PdlSpec(ctypes.Structure):
+    _fields_ = [("max_batch", _i32), ("num_heads", _i32), ("num_kv_heads", _i32),
+                ("head_dim", _i32), ("max_context_len", _i32), ("page_size", _i32)]
+
+
+class PdlPlan(ctypes.Structure):
+    _fields_ = [("splits", _i32), ("tile_tokens", _i32), ("tokens_per_split", _i32),
+                ("table_capacity_tokens", _i32), ("lse_lanes", _i32), ("sm_count", _i32),
+                ("explicit_splits", _i32)]
+
+
+class PdlDecodeArgs(ctypes.Structure):
+    _fields_ = [("q", _vp), ("q_stride_batch", _i64), ("q_stride_head", _i64),
+                ("k_cache", _vp), ("v_cache", _vp), ("num_pages", _i64),
+                ("block_table", _vp), ("table_stride", _i64), ("table_width", _i32),
+                ("lengths", _vp), ("batch", _i32), ("num_heads", _i32),
+                ("num_kv_heads", _i32), ("head_dim", _i32), ("scale", _f32),
+                ("tokens_per_split", _i32), ("splits", _i32), ("protocol", _i32),
+                ("kernel", _i32), ("flags", _i32), ("out", _vp), ("partial", _vp),
+                ("lse", _vp), ("maxima", _vp), ("denoms", _vp), ("accums", _vp)]
+
+
+_LIB = None
+
+
+def load():
+    """Load the library once; raise with a build hint when it is absent."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIBRARY.exists():
+        raise RuntimeError(
+            f"paged-decode CUDA library not found at {LIBRARY}; build it with "
+            "`python paged-decode-lab_b200/csrc/build.py` (no CPU fallback exists)")
+    lib = ctypes.CDLL(str(LIBRARY))
+    args_p = ctypes.POINTER(PdlDecodeArgs)
+    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode"):
+        fn = getattr(lib, name)
+        fn.argtypes = [args_p, _vp]
+        fn.restype = ctypes.c_int
+    lib.pdl_splitkv_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, _i32, ctypes.POINTER(PdlPlan)]
+    lib.pdl_splitkv_plan.restype = ctypes.c_int
+    lib.pdl_spec_geometry.argtypes = [ctypes.POINTER(PdlSpec), ctypes.POINTER(_i32),
+                                      ctypes.POINTER(_i32), ctypes.POINTER(_i64)]
+    lib.pdl_spec_geometry.restype = ctypes.c_int
+    lib.pdl_status_string.argtypes = [ctypes.c_int]
+    lib.pdl_status_string.restype = ctypes.c_char_p
+    lib.pdl_last_error.argtypes = []
+    lib.pdl_last_error.restype = ctypes.c_char_p
+    lib.pdl_abi_version.argtypes = []
+    lib.pdl_abi_version.restype = ctypes.c_int
+    lib.pdl_read_fault.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
+    lib.pdl_read_fault.restype = ctypes.c_int
+    version = lib.pdl_abi_version()
+    if version != ABI_VERSION:
+        raise RuntimeError(f"{LIBRARY} has ABI {version}, expected {ABI_VERSION}; rebuild it")
+    _LIB = lib
+    return lib
+
+
+def status_text(status):
+    lib = load()
+    text = f"{STATUS_NAMES.get(status, status)}: {lib.pdl_status_string(status).decode()}"
+    detail = lib.pdl_last_error().decode()
+    return f"{text} ({detail})" if detail else text
+
+
+def make_spec(spec):
+    return PdlSpec(spec.max_batch, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                   spec.max_context_len, spec.page_size)
+
+
+def read_fault(clear=False):
+    """Sticky device-side fault word of the current device (synchronises)."""
+    word = ctypes.c_uint32(0)
+    status = load().pdl_read_fault(ctypes.byref(word), int(clear))
+    if status != PDL_OK:
+        raise RuntimeError(f"pdl_read_fault failed: {status_text(status)}")
+    return word.value

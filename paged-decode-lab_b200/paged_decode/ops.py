@@ -1,0 +1,94 @@
+"""Tensor-level wrappers over the C ABI (no validation beyond the library's).
+
+These take torch tensors that already satisfy the contract (device, dtype,
+layout), fill one ``PdlDecodeArgs`` and enqueue on the current CUDA stream
+of the tensors' device.  ``runtime.paged_decode`` and
+``matched_splitkv.matched_decode`` validate with the reference's messages
+first and then call these.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+PROTOCOL_LSE = _lib.PROTOCOL_LSE
+PROTOCOL_MLA = _lib.PROTOCOL_MLA
+KERNEL_AUTO = _lib.KERNEL_AUTO
+KERNEL_SIMT = _lib.KERNEL_SIMT
+KERNEL_MMA = _lib.KERNEL_MMA
+FLAG_SKIP_EMPTY = _lib.FLAG_SKIP_EMPTY
+FLAG_DIRECT_SINGLE = _lib.FLAG_DIRECT_SINGLE
+
+_KERNELS = {"auto": KERNEL_AUTO, "simt": KERNEL_SIMT, "mma": KERNEL_MMA}
+
+
+def _addr(t):
+    return None if t is None else t.data_ptr()
+
+
+def decode_args(q, k, v, tables, lengths, *, scale, tokens_per_split=0, splits=1,
+                protocol=PROTOCOL_LSE, kernel="auto", flags=0, out=None, partial=None,
+                lse=None, maxima=None, denoms=None, accums=None):
+    """Fill a ``PdlDecodeArgs`` from tensors (element strides, raw addresses)."""
+    a = _lib.PdlDecodeArgs()
+    a.q = q.data_ptr()
+    a.q_stride_batch = q.stride(0)
+    a.q_stride_head = q.stride(1)
+    a.k_cache = k.data_ptr()
+    a.v_cache = v.data_ptr()
+    a.num_pages = k.shape[0]
+    a.block_table = tables.data_ptr()
+    a.table_stride = tables.stride(0)
+    a.table_width = tables.shape[1]
+    a.lengths = lengths.data_ptr()
+    a.batch = q.shape[0]
+    a.num_heads = q.shape[1]
+    a.num_kv_heads = k.shape[2]
+    a.head_dim = q.shape[2]
+    a.scale = float(scale)
+    a.tokens_per_split = int(tokens_per_split)
+    a.splits = int(splits)
+    a.protocol = protocol
+    a.kernel = _KERNELS[kernel] if isinstance(kernel, str) else int(kernel)
+    a.flags = int(flags)
+    a.out = _addr(out)
+    a.partial = _addr(partial)
+    a.lse = _addr(lse)
+    a.maxima = _addr(maxima)
+    a.denoms = _addr(denoms)
+    a.accums = _addr(accums)
+    return a
+
+
+def _call(name, args, device):
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        status = getattr(lib, name)(ctypes.byref(args), ctypes.c_void_p(stream))
+    if status != _lib.PDL_OK:
+        raise RuntimeError(f"{name} failed: {_lib.status_text(status)}")
+
+
+def partition(args, device):
+    """Launch the partition kernel (``pdl_partition``)."""
+    _call("pdl_partition", args, device)
+
+
+def merge(args, device):
+    """Launch the merge kernel (``pdl_merge``)."""
+    _call("pdl_merge", args, device)
+
+
+def paged_decode(args, device):
+    """Partition + merge, or the single-pass kernel (``pdl_paged_decode``)."""
+    _call("pdl_paged_decode", args, device)
+
+
+def read_fault(clear=False):
+    """Device-side fault word (bounded waits that gave up); synchronises."""
+    return _lib.read_fault(clear)
+
+
+def sm_count(device):
+    return torch.cuda.get_device_properties(torch.device(device)).multi_processor_count

@@ -1,0 +1,155 @@
+"""CPU tests of the C ABI and the host-side logic (no GPU calls).
+
+* the shared library loads and exports every symbol ``include/pdl_b200.h`` declares;
+* the native plan / geometry equal the reference's golden values exactly;
+* ``DecodeSpec`` and the engine-option checks keep the reference's contract
+  (reference tests/test_reference.py:60-81, tests/test_splitkv_plan.py).
+"""
+import ctypes
+import json
+import re
+from pathlib import Path
+
+import pytest
+
+import oracle
+from paged_decode import _lib
+from paged_decode.spec import DecodeSpec, validate_engine_options
+from paged_decode.splitkv_plan import make_splitkv_plan
+from paged_decode.benchmark_protocol import interval_per_operator, convergence_delta
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "pdl_b200.h"
+PLANS = json.loads((ROOT / "tests" / "golden" / "golden_plans.json").read_text())
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|const char \*)\s*(pdl_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert names == sorted(_lib.SYMBOLS)
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.pdl_abi_version() == _lib.ABI_VERSION
+
+
+def test_status_strings():
+    lib = _lib.load()
+    assert lib.pdl_status_string(0) == b"ok"
+    assert b"workspace" in lib.pdl_status_string(4)
+    assert lib.pdl_status_string(999) == b"unknown status"
+
+
+def test_native_plan_matches_reference_golden():
+    lib = _lib.load()
+    fields = PLANS["plan_fields"]
+    for row in PLANS["plans"]:
+        rec = dict(zip(fields, row))
+        spec = _lib.PdlSpec(rec["max_batch"], rec["num_heads"], rec["num_kv_heads"],
+                            rec["head_dim"], rec["max_context_len"], 256)
+        plan = _lib.PdlPlan()
+        assert lib.pdl_splitkv_plan(ctypes.byref(spec), rec["sm_count"], rec["num_splits"],
+                                    ctypes.byref(plan)) == 0
+        got = [plan.splits, plan.tile_tokens, plan.tokens_per_split, plan.table_capacity_tokens,
+               plan.lse_lanes, "explicit" if plan.explicit_splits else "pinned_geometry"]
+        assert got == row[7:], rec
+
+
+def test_native_plan_matches_oracle_on_unseen_specs():
+    for batch in (1, 5, 17, 64, 100, 300):
+        for hq, hkv in ((12, 4), (16, 2), (40, 8), (64, 4)):
+            for dim in (64, 128, 256):
+                for cap in (100, 777, 4096, 40000):
+                    for sms in (132, 148, 160):
+                        spec = DecodeSpec(batch, hq, hkv, dim, cap)
+                        got = make_splitkv_plan(spec, sms)
+                        want = oracle.make_splitkv_plan(batch, hq, hkv, dim, cap, sms)
+                        assert (got.splits, got.tokens_per_split, got.lse_lanes) == \
+                            (want.splits, want.tokens_per_split, want.lse_lanes)
+
+
+def test_native_geometry_matches_reference_golden():
+    lib = _lib.load()
+    for rec in PLANS["geometry"]:
+        b, hq, hkv, d, cap = rec["spec"]
+        parts, width, ws = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
+        spec = _lib.PdlSpec(b, hq, hkv, d, cap, 256)
+        assert lib.pdl_spec_geometry(ctypes.byref(spec), ctypes.byref(parts), ctypes.byref(width),
+                                     ctypes.byref(ws)) == 0
+        assert (parts.value, width.value, ws.value) == \
+            (rec["partitions"], rec["table_width"], rec["split_workspace_bytes"])
+        py = DecodeSpec(b, hq, hkv, d, cap)
+        assert (py.partitions, py.table_width, py.split_workspace_bytes) == \
+            (rec["partitions"], rec["table_width"], rec["split_workspace_bytes"])
+
+
+def test_native_geometry_rejects_bad_specs():
+    lib = _lib.load()
+    for bad in ((0, 8, 2, 128, 10), (1, 8, 3, 128, 10), (1, 8, 2, 80, 10)):
+        spec = _lib.PdlSpec(*bad, 256)
+        assert lib.pdl_spec_geometry(ctypes.byref(spec), None, None, None) != 0
+    spec = _lib.PdlSpec(1, 8, 2, 128, 10, 16)
+    assert lib.pdl_spec_geometry(ctypes.byref(spec), None, None, None) == 2
+
+
+def test_launch_entry_points_reject_null_args_without_a_gpu():
+    lib = _lib.load()
+    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode"):
+        assert getattr(lib, name)(None, None) == 1
+
+
+def test_spec_and_memory():
+    spec = DecodeSpec(32, 32, 8, 128, 8192)
+    assert spec.partitions == 8
+    assert spec.table_width == 32
+    assert spec.split_workspace_bytes == 32 * 32 * 8 * 130 * 4
+
+
+@pytest.mark.parametrize("kwargs", [{"head_dim": 80}, {"page_size": 16}, {"num_kv_heads": 3},
+                                    {"max_batch": 0}, {"max_context_len": -1}])
+def test_unsupported_geometry(kwargs):
+    values = dict(max_batch=8, num_heads=4, num_kv_heads=2, head_dim=64, max_context_len=2048)
+    values.update(kwargs)
+    with pytest.raises(ValueError):
+        DecodeSpec(**values)
+
+
+@pytest.mark.parametrize("backend,tp,page", [("typo", 1, 256), ("triton_base", 2, 256),
+                                            ("triton_splitk", 1, 512)])
+def test_engine_rejects_unsupported_options(backend, tp, page):
+    with pytest.raises(ValueError):
+        validate_engine_options(backend, tp, page, 32, 8192)
+
+
+def test_explicit_count_partitions_capacity_in_tiles():
+    plan = make_splitkv_plan(DecodeSpec(1, 16, 4, 256, 2176), 108, num_splits=3)
+    assert plan.splits == 3 and plan.tokens_per_split == 768
+    assert plan.policy == "explicit"
+
+
+@pytest.mark.parametrize("count", [-1, 129, 1.5])
+def test_unsupported_explicit_counts(count):
+    with pytest.raises(ValueError, match="num_splits"):
+        make_splitkv_plan(DecodeSpec(1, 8, 2, 256, 1024), 108, num_splits=count)
+
+
+def test_unsupported_group():
+    with pytest.raises(ValueError, match="16"):
+        make_splitkv_plan(DecodeSpec(1, 32, 1, 256, 1024), 108)
+
+
+def test_graph_nodes_are_counted_as_logical_operators():
+    assert interval_per_operator(1.28, 10, 128) == 1.
+    assert interval_per_operator(1.28, 1280, 1) == 1.
+    assert convergence_delta(10.4, 10.) == pytest.approx(.04)
+
+
+@pytest.mark.parametrize('args', [(0., 10, 128), (float('nan'), 10, 128), (1., 0, 128),
+                                  (1., 10, 0), (1., 10, True)])
+def test_invalid_denominators_cannot_produce_latency(args):
+    with pytest.raises(ValueError):
+        interval_per_operator(*args)
