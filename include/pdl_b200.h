@@ -149,6 +149,26 @@ int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream);
  * (src/paged_decode/tc_splitk.py:63-79). */
 int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream);
 
+/* Capacity of the device array used by pdl_paged_decode_static_scratch. */
+#define PDL_STATIC_SCRATCH_BYTES (4u << 20)
+
+/* pdl_paged_decode without a caller-provided workspace, for callers that
+ * cannot allocate device memory: an engine that has reserved nearly all HBM
+ * for its KV page pool, a host behind an FFI that only holds pointers the
+ * engine gave it, or a path that must not call cudaMalloc/cudaFree because
+ * they can synchronise the device.  No counterpart in the reference.
+ * The partial + LSE workspace is a file-scope __device__ array of
+ * PDL_STATIC_SCRATCH_BYTES (4 MiB) that every GPU loading the library holds
+ * until exit; calls needing batch*num_heads*splits*(head_dim+1)*4 bytes
+ * beyond that are rejected with PDL_ERR_WORKSPACE (pdl_last_error says how
+ * much was needed).  The workspace pointers and protocol in `args` are
+ * ignored (LSE protocol).  The first call on a device looks up the array's
+ * device address with that device current; make that first call before any
+ * stream capture.  All calls on a device share the array and it keeps the
+ * last call's contents (nothing in it needs to start at zero), so calls
+ * that overlap on the GPU race.  Nothing is allocated. */
+int pdl_paged_decode_static_scratch(const PdlDecodeArgs *args, pdl_stream_t stream);
+
 /* Static plan for `spec` on `sm_count` SMs; num_splits 0 = heuristic.
  * Replaces make_splitkv_plan (reference src/paged_decode/splitkv_plan.py:26-56). */
 int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,

@@ -409,3 +409,83 @@ extern "C" int pdl_read_fault(uint32_t *fault, int clear) {
   if (clear && cudaMemset(dev->fault, 0, sizeof(uint32_t)) != cudaSuccess) return PDL_ERR_CUDA;
   return PDL_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode: pdl_paged_decode_static_scratch.
+//
+// Some callers cannot allocate device memory for the split workspace: an
+// engine that reserved (nearly) all free HBM for its KV page pool at start-up
+// and leaves no room for extra buffers, a host that reaches this library
+// through an FFI and only holds device pointers handed to it by an engine
+// that owns every allocation, or a code path that must not call cudaMalloc /
+// cudaFree because those calls can synchronise the whole device.  For them
+// the partial + LSE workspace lives in the file-scope device array below,
+// which every GPU that loads this library keeps until the process exits.
+//
+// The caller still passes q, K/V, table, lengths and the output; the
+// workspace pointers in PdlDecodeArgs are ignored.  The array is shared by
+// all calls on a device and keeps the last call's contents; nothing in it
+// has to start at zero, because the partition kernel stores every partition
+// the merge reads.  Two calls whose work overlaps on the GPU (different
+// streams, or graphs replayed concurrently) race on the array.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_pdl_static_scratch[PDL_STATIC_SCRATCH_BYTES / sizeof(float)];
+
+namespace pdl {
+namespace {
+
+float *g_static_scratch[kMaxDevices];  // device address of the array, per device
+std::mutex g_static_scratch_mutex;
+
+// Set up once per device, with that device current: the host-side name of a
+// __device__ array is only a stand-in, so its device address is fetched with
+// cudaGetSymbolAddress and passed to the kernels.
+int static_scratch_for_current_device(float **out) {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDevices) return PDL_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch[dev] == nullptr) {
+    void *addr = nullptr;
+    const cudaError_t r = cudaGetSymbolAddress(&addr, g_pdl_static_scratch);
+    if (r != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(static scratch)", r);
+    g_static_scratch[dev] = static_cast<float *>(addr);
+  }
+  *out = g_static_scratch[dev];
+  return PDL_OK;
+}
+
+}  // namespace
+}  // namespace pdl
+
+extern "C" int pdl_paged_decode_static_scratch(const PdlDecodeArgs *args, pdl_stream_t stream) {
+  int st = validate_common(args);
+  if (st == PDL_OK) st = validate_partition_inputs(args);
+  if (st == PDL_OK) st = validate_out(args);
+  if (st != PDL_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (args->tokens_per_split == 0) return run_partition(args, MODE_DIRECT, s);  // no workspace
+  const int64_t rows = (int64_t)args->batch * args->num_heads * args->splits;
+  const int64_t bytes = rows * (args->head_dim + 1) * (int64_t)sizeof(float);
+  if (bytes > (int64_t)PDL_STATIC_SCRATCH_BYTES) {
+    char detail[160];
+    snprintf(detail, sizeof(detail),
+             "needs %lld bytes of scratch (batch*num_heads*splits*(head_dim+1)*4); "
+             "the static scratch holds %lld",
+             (long long)bytes, (long long)PDL_STATIC_SCRATCH_BYTES);
+    return fail(PDL_ERR_WORKSPACE, "pdl_paged_decode_static_scratch", detail);
+  }
+  float *scratch = nullptr;
+  st = static_scratch_for_current_device(&scratch);
+  if (st != PDL_OK) return st;
+  PdlDecodeArgs a = *args;
+  a.protocol = PDL_PROTOCOL_LSE;
+  a.partial = scratch;
+  a.lse = scratch + rows * args->head_dim;  // 256-byte aligned: head_dim is a multiple of 64
+  a.maxima = a.denoms = a.accums = nullptr;
+  if (a.splits == 1 && (a.flags & PDL_FLAG_DIRECT_SINGLE)) return run_partition(&a, MODE_DIRECT, s);
+  st = run_partition(&a, MODE_LSE, s);
+  if (st != PDL_OK) return st;
+  return run_merge(&a, s);
+}

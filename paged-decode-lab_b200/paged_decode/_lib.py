@@ -21,9 +21,10 @@ KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
 FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE = 1, 2
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
-SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_paged_decode", "pdl_splitkv_plan",
-           "pdl_spec_geometry", "pdl_status_string", "pdl_last_error", "pdl_abi_version",
-           "pdl_read_fault")
+SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_paged_decode", "pdl_paged_decode_static_scratch",
+           "pdl_splitkv_plan", "pdl_spec_geometry", "pdl_status_string", "pdl_last_error",
+           "pdl_abi_version", "pdl_read_fault")
+STATIC_SCRATCH_BYTES = 4 << 20
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -64,7 +65,8 @@ def load():
             "`python paged-decode-lab_b200/csrc/build.py` (no CPU fallback exists)")
     lib = ctypes.CDLL(str(LIBRARY))
     args_p = ctypes.POINTER(PdlDecodeArgs)
-    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode"):
+    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode",
+                 "pdl_paged_decode_static_scratch"):
         fn = getattr(lib, name)
         fn.argtypes = [args_p, _vp]
         fn.restype = ctypes.c_int

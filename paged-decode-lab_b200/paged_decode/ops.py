@@ -85,6 +85,17 @@ def paged_decode(args, device):
     _call("pdl_paged_decode", args, device)
 
 
+def paged_decode_static_scratch(args, device):
+    """``pdl_paged_decode_static_scratch``: decode without a caller workspace.
+
+    For callers that cannot allocate device memory (an engine that reserved
+    nearly all HBM for its KV pool, or a path that must not call
+    cudaMalloc/cudaFree); the workspace is the library's 4 MiB device array,
+    shared by every call on the device.  Larger requests raise.
+    """
+    _call("pdl_paged_decode_static_scratch", args, device)
+
+
 def read_fault(clear=False):
     """Device-side fault word (bounded waits that gave up); synchronises."""
     return _lib.read_fault(clear)
