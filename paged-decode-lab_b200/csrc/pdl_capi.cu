@@ -110,6 +110,41 @@ int encode_pool_map(CUtensorMap *map, const void *base, int64_t pages, int hkv, 
   return PDL_OK;
 }
 
+// Encoded descriptors are cached per host thread: a decode loop reuses the
+// same pools call after call, and encoding is pure host work.
+struct PoolMapEntry {
+  const void *base;
+  int64_t pages;
+  int hkv, dim, box;
+  CUtensorMap map;
+};
+constexpr int kPoolMapCache = 8;
+thread_local PoolMapEntry g_pool_maps[kPoolMapCache];
+thread_local int g_pool_map_next = 0;
+
+int cached_pool_map(CUtensorMap *map, const void *base, int64_t pages, int hkv, int dim,
+                    int box_tokens) {
+  for (int i = 0; i < kPoolMapCache; ++i) {
+    const PoolMapEntry &e = g_pool_maps[i];
+    if (e.base == base && base != nullptr && e.pages == pages && e.hkv == hkv && e.dim == dim &&
+        e.box == box_tokens) {
+      *map = e.map;
+      return PDL_OK;
+    }
+  }
+  const int st = encode_pool_map(map, base, pages, hkv, dim, box_tokens);
+  if (st != PDL_OK) return st;
+  PoolMapEntry &slot = g_pool_maps[g_pool_map_next];
+  g_pool_map_next = (g_pool_map_next + 1) % kPoolMapCache;
+  slot.base = base;
+  slot.pages = pages;
+  slot.hkv = hkv;
+  slot.dim = dim;
+  slot.box = box_tokens;
+  slot.map = *map;
+  return PDL_OK;
+}
+
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 bool valid_dim(int d) { return d == 64 || d == 128 || d == 256; }
@@ -195,9 +230,9 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   if (items > INT32_MAX) return PDL_ERR_SHAPE;
 
   CUtensorMap kmap, vmap;
-  st = encode_pool_map(&kmap, a->k_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
+  st = cached_pool_map(&kmap, a->k_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
   if (st != PDL_OK) return st;
-  st = encode_pool_map(&vmap, a->v_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
+  st = cached_pool_map(&vmap, a->v_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
   if (st != PDL_OK) return st;
 
   KernelLaunch L;

@@ -68,7 +68,7 @@ def load():
     for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode",
                  "pdl_paged_decode_static_scratch"):
         fn = getattr(lib, name)
-        fn.argtypes = [args_p, _vp]
+        fn.argtypes = [args_p, ctypes.c_size_t]  # stream handle as an integer
         fn.restype = ctypes.c_int
     lib.pdl_splitkv_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, _i32, ctypes.POINTER(PdlPlan)]
     lib.pdl_splitkv_plan.restype = ctypes.c_int

@@ -48,6 +48,13 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
     head serves >= 8 query heads, CUDA cores otherwise), "simt" or "mma".
     """
     scale = q.shape[-1] ** -.5 if scale is None else float(scale)
+    cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
+    key = ((kernel, scale, q.device) + ops.tensor_key(q, k, v, tables, lengths)
+           + ops.buffers_key(resources.out, resources.partials, resources.lse))
+    args = cache.get(key)
+    if args is not None:
+        ops.paged_decode(args, q.device)
+        return resources.out
     _validate(q, k, v, tables, lengths, resources, "triton_base", scale)
     if scale <= 0 or not math.isfinite(scale):
         raise ValueError("positive finite scale required")
@@ -65,4 +72,5 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
                            protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
                            partial=resources.partials, lse=resources.lse)
     ops.paged_decode(args, q.device)
+    cache.put(key, args)
     return resources.out

@@ -62,12 +62,44 @@ def decode_args(q, k, v, tables, lengths, *, scale, tokens_per_split=0, splits=1
 
 
 def _call(name, args, device):
-    lib = _lib.load()
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device).cuda_stream
-        status = getattr(lib, name)(ctypes.byref(args), ctypes.c_void_p(stream))
+    fn = getattr(_lib.load(), name)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if torch.cuda.current_device() == index:
+        status = fn(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
+    else:
+        with torch.cuda.device(index):
+            status = fn(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
     if status != _lib.PDL_OK:
         raise RuntimeError(f"{name} failed: {_lib.status_text(status)}")
+
+
+def tensor_key(*tensors):
+    """Metadata that fixes a launch: addresses, shapes, strides and dtypes.
+
+    Validation depends only on these, never on tensor contents, so a launch
+    whose key was validated once may reuse its filled ``PdlDecodeArgs``.
+    """
+    key = []
+    for t in tensors:
+        key.extend((t.data_ptr(), t.shape, t.stride(), t.dtype))
+    return tuple(key)
+
+
+def buffers_key(*tensors):
+    """Addresses of output / workspace buffers (None where absent)."""
+    return tuple(None if t is None else t.data_ptr() for t in tensors)
+
+
+class LaunchCache(dict):
+    """Bounded map from launch keys to validated ``PdlDecodeArgs``."""
+
+    LIMIT = 64
+
+    def put(self, key, args):
+        if len(self) >= self.LIMIT:
+            self.clear()
+        self[key] = args
+        return args
 
 
 def partition(args, device):

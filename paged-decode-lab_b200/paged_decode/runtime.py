@@ -133,6 +133,13 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
     Padding table entries may contain -1 (never read).
     """
     scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
+    key = ((backend, scale, q.device) + ops.tensor_key(q, k, v, tables, lengths)
+           + ops.buffers_key(resources.out, resources.maxima, resources.denoms, resources.accums))
+    args = cache.get(key)
+    if args is not None:
+        ops.paged_decode(args, q.device)
+        return resources.out[:q.shape[0]]
     if backend not in _CUSTOM:
         raise ValueError("unknown custom backend")
     split = backend in ("triton_splitk", "triton_tc_splitk")
@@ -160,4 +167,5 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)
     ops.paged_decode(args, q.device)
+    cache.put(key, args)
     return resources.out[:q.shape[0]]

@@ -98,8 +98,9 @@ def test_native_geometry_rejects_bad_specs():
 
 def test_launch_entry_points_reject_null_args_without_a_gpu():
     lib = _lib.load()
-    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode"):
-        assert getattr(lib, name)(None, None) == 1
+    for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode",
+                 "pdl_paged_decode_static_scratch"):
+        assert getattr(lib, name)(None, 0) == 1
 
 
 def test_spec_and_memory():

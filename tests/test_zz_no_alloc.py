@@ -29,7 +29,7 @@ def _call(entry, args, device):
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        return getattr(lib, entry)(ctypes.byref(args), ctypes.c_void_p(stream))
+        return getattr(lib, entry)(ctypes.byref(args), stream)
 
 
 def _with_workspace(q, k, v, table, lens, splits, tokens):
