@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--context", type=int, default=None)
     ap.add_argument("--splits", type=int, default=None, help="matched plan split count")
     ap.add_argument("--kernel", default="auto", choices=("auto", "simt", "mma"))
+    ap.add_argument("--mode", default="batch", choices=("batch", "context"),
+                    help="N>1: independent batch per rank (weak) or one batch split by context "
+                         "across ranks with an NCCL all-gather (strong)")
     ap.add_argument("--window-seconds", type=float, default=0.5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -238,29 +241,55 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    context = args.mode == "context" and world > 1
+    # Context mode: every rank builds the same global batch and keeps its page range.
     first = make_workload(args.config, device=device, batch=args.batch, context=args.context,
-                          rank=rank)
-    pool_bytes = first.k.numel() * 2 * 2
-    copies = 1 if pool_bytes >= 2 * L2_BYTES else min(64, math.ceil(2 * L2_BYTES / pool_bytes))
-    wls = [first] + [make_workload(args.config, device=device, batch=args.batch,
-                                   context=args.context, rank=rank, seed=c)
-                     for c in range(1, copies)]
-    res = allocate_matched_resources(first.spec, device,
-                                     num_splits=config_splits(args.config, args))
+                          rank=0 if context else rank)
     kv_bytes = first.kv_bytes  # every copy has the same lengths
     stream = torch.cuda.current_stream(device)
     K = args.steps
+    if context:
+        from paged_decode import parallel
+        k_loc, v_loc, t_loc = parallel.shard_context_pool(first.k, first.v, first.table, rank,
+                                                          world)
+        first.k, first.v, first.table = k_loc, v_loc, t_loc
+        torch.cuda.empty_cache()
+        cp = parallel.ContextParallelDecode(first.spec, device, kernel=args.kernel,
+                                            local_splits=config_splits(args.config, args))
+        copies, wls = 1, [first]
+        cp(first.q, k_loc, v_loc, t_loc, first.lengths)
+        plan = cp.plan
+        local_bytes = int(cp.local_len.sum().item()) * first.spec.num_kv_heads * \
+            first.spec.head_dim * 4
+
+        def decode_call(w):
+            return cp(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale)
+
+        part_args = [cp._launch_args(first.q, k_loc, v_loc, t_loc, first.scale)[0]]
+        out_buf = cp.out
+    else:
+        pool_bytes = first.k.numel() * 2 * 2
+        copies = 1 if pool_bytes >= 2 * L2_BYTES else min(64, math.ceil(2 * L2_BYTES / pool_bytes))
+        wls = [first] + [make_workload(args.config, device=device, batch=args.batch,
+                                       context=args.context, rank=rank, seed=c)
+                         for c in range(1, copies)]
+        res = allocate_matched_resources(first.spec, device,
+                                         num_splits=config_splits(args.config, args))
+        plan = res.plan
+        local_bytes = kv_bytes
+
+        def decode_call(w):
+            return matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res,
+                                  scale=w.scale, kernel=args.kernel)
+
+        part_args = [ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
+                                     tokens_per_split=plan.tokens_per_split, splits=plan.splits,
+                                     protocol=ops.PROTOCOL_LSE, kernel=args.kernel, out=res.out,
+                                     partial=res.partials, lse=res.lse) for w in wls]
+        out_buf = res.out
 
     def step(i):
-        w = wls[i % copies]
-        matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res, scale=w.scale,
-                       kernel=args.kernel)
-
-    plan = res.plan
-    part_args = [ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
-                                 tokens_per_split=plan.tokens_per_split, splits=plan.splits,
-                                 protocol=ops.PROTOCOL_LSE, kernel=args.kernel, out=res.out,
-                                 partial=res.partials, lse=res.lse) for w in wls]
+        decode_call(wls[i % copies])
 
     def partition_only(i):
         ops.partition(part_args[i % copies], device)
@@ -308,13 +337,14 @@ def main():
     step_graph = capture(step)
     total_ms, reps = timed(step_graph, args.window_seconds)
     ms_per_step = total_ms / (reps * K)
-    value = world * kv_bytes / (ms_per_step / 1e3) / 1e9
+    job_bytes = kv_bytes if context else world * kv_bytes
+    value = job_bytes / (ms_per_step / 1e3) / 1e9
 
     part_graph = capture(partition_only)
     part_total, part_reps = timed(part_graph, args.window_seconds / 2)
     part_ms = part_total / (part_reps * K)
     peak, peak_src = measured_peak()
-    achieved = kv_bytes / (part_ms / 1e3) / 1e9
+    achieved = local_bytes / (part_ms / 1e3) / 1e9
     group = first.spec.num_heads // first.spec.num_kv_heads
     kernel_name = "mma" if (args.kernel == "mma" or (args.kernel == "auto" and group >= 8)) \
         else "simt"
@@ -326,7 +356,7 @@ def main():
         hq = torch.empty(w.q.shape, dtype=w.q.dtype).pin_memory()
         hq.copy_(w.q)
         hosts.append((hq, w.table.cpu().pin_memory(), w.lengths.cpu().pin_memory()))
-    hout = torch.empty(res.out.shape, dtype=res.out.dtype).pin_memory()
+    hout = torch.empty(out_buf.shape, dtype=out_buf.dtype).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in hosts[0])
     d2h = hout.numel() * hout.element_size()
 
@@ -335,9 +365,7 @@ def main():
         w.q.copy_(hq, non_blocking=True)
         w.table.copy_(ht, non_blocking=True)
         w.lengths.copy_(hl, non_blocking=True)
-        out = matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res, scale=w.scale,
-                             kernel=args.kernel)
-        hout.copy_(out, non_blocking=True)
+        hout.copy_(decode_call(w), non_blocking=True)
 
     for i in range(3):
         e2e_step(i)
@@ -351,7 +379,7 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize(device)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = world * kv_bytes * K / (e2e_ms / 1e3) / 1e9
+    e2e_value = job_bytes * K / (e2e_ms / 1e3) / 1e9
     fault = ops.read_fault()
     clocks.stop()
 
@@ -360,7 +388,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
             "us_per_call": round(ms_per_step * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, fp32 softmax/accumulate",
+            "scaling": "strong" if context else "weak", "vs_baseline": None,
+            "dtype": "bf16 in, fp32 softmax/accumulate",
             "data": "synthetic (seeded N(0,1) BF16 q/K/V, shuffled page pool)",
             "config": {"workload": args.config, "batch": first.spec.max_batch,
                        "num_heads": first.spec.num_heads,
@@ -368,7 +397,9 @@ def main():
                        "head_dim": first.spec.head_dim, "context": first.spec.max_context_len,
                        "splits": plan.splits, "tokens_per_split": plan.tokens_per_split,
                        "kv_bytes_per_step": kv_bytes, "kernel": kernel_name,
-                       "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"context-parallel x{world} (NCCL all-gather + LSE merge)"
+                                       if context else f"batch-sharded x{world}" if world > 1
+                                       else "single GPU"),
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",
                        "l2": ("inputs larger than L2 (KV pool >> 126 MB)" if copies == 1 else
                               f"{copies} independent input copies rotated (> 2x L2)")},
@@ -379,8 +410,9 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_call": round(e2e_ms / K * 1e3, 3),
-                    "api": "paged_decode.matched_splitkv.matched_decode"},
-            "gpu_launches": 2 * K * reps,
+                    "api": ("paged_decode.parallel.ContextParallelDecode" if context
+                            else "paged_decode.matched_splitkv.matched_decode")},
+            "gpu_launches": (5 if context else 2) * K * reps,
             "clocks": clocks.summary(windows),
             "fault_word": fault,
         }

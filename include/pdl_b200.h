@@ -142,6 +142,35 @@ int pdl_partition(const PdlDecodeArgs *args, pdl_stream_t stream);
  * _merge (src/paged_decode/kernels.py:83-100). */
 int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream);
 
+/* Strided LSE merge: rows r = 0..rows-1, partitions p = 0..parts-1 with
+ *   partial row at partial[r*row_stride + p*part_stride]   (head_dim floats)
+ *   lse         at lse[r*lse_row_stride + p*lse_part_stride].
+ * Covers the split workspace (row_stride = parts*D, part_stride = D) and the
+ * rank-major buffer of an all-gather (row_stride = D, part_stride = the
+ * per-rank block).  Strides are in floats. */
+typedef struct PdlMergeArgs {
+  const float *partial;
+  const float *lse;
+  int64_t row_stride;
+  int64_t part_stride;
+  int64_t lse_row_stride;
+  int64_t lse_part_stride;
+  int32_t rows;               /* batch * num_heads */
+  int32_t parts;
+  int32_t head_dim;
+  void *out;                  /* bf16 [rows, head_dim], or NULL                  */
+  float *out_partial;         /* f32 [rows, head_dim] merged partial, or NULL    */
+  float *out_lse;             /* f32 [rows] merged LSE (-inf if empty), or NULL  */
+} PdlMergeArgs;
+
+/* Stable LSE merge of arbitrary-strided partitions into a BF16 output and/or
+ * an FP32 (partial, LSE) pair that can feed a further merge (the
+ * context-parallel combine after an all-gather).  Same arithmetic as
+ * _lse_merge (reference src/paged_decode/matched_splitkv.py:101-127); the
+ * strided layout and the (partial, LSE) output have no counterpart in the
+ * reference, which has no multi-GPU path. */
+int pdl_lse_merge(const PdlMergeArgs *args, pdl_stream_t stream);
+
 /* Partition + merge (or the single-pass kernel when tokens_per_split == 0).
  * Replaces the launch sequence of paged_decode (reference
  * src/paged_decode/runtime.py:87-117), matched_decode

@@ -289,6 +289,10 @@ int run_merge(const PdlDecodeArgs *a, cudaStream_t stream) {
   m.rows = a->batch * a->num_heads;
   m.splits = a->splits;
   m.protocol = a->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA;
+  m.row_stride = (int64_t)a->splits * a->head_dim;
+  m.part_stride = a->head_dim;
+  m.w_row_stride = a->splits;
+  m.w_part_stride = 1;
   return status_from_cuda(launch_merge(m, a->head_dim, stream), "merge");
 }
 
@@ -415,6 +419,37 @@ extern "C" int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream) {
   if (st == PDL_OK) st = validate_out(args);
   if (st != PDL_OK) return st;
   return run_merge(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pdl_lse_merge(const PdlMergeArgs *args, pdl_stream_t stream) {
+  if (args == nullptr || args->partial == nullptr || args->lse == nullptr) return PDL_ERR_NULL;
+  if (!valid_dim(args->head_dim)) return PDL_ERR_GEOMETRY;
+  if (args->rows <= 0 || args->parts <= 0) return PDL_ERR_SHAPE;
+  if (!args->out && !args->out_partial && !args->out_lse) return PDL_ERR_NULL;
+  // Every partition row must start on a 16-byte boundary for vector loads.
+  if (!aligned(args->partial, 16) || args->row_stride % 4 || args->part_stride % 4)
+    return PDL_ERR_ALIGNMENT;
+  if ((args->out && !aligned(args->out, 16)) ||
+      (args->out_partial && !aligned(args->out_partial, 16)))
+    return PDL_ERR_ALIGNMENT;
+  MergeParams m;
+  std::memset(&m, 0, sizeof(m));
+  m.partial = args->partial;
+  m.lse = args->lse;
+  m.row_stride = args->row_stride;
+  m.part_stride = args->part_stride;
+  m.w_row_stride = args->lse_row_stride;
+  m.w_part_stride = args->lse_part_stride;
+  m.out = static_cast<__nv_bfloat16 *>(args->out);
+  m.out_partial = args->out_partial;
+  m.out_lse = args->out_lse;
+  m.num_heads = 1;
+  m.tokens_per_split = 1 << 30;
+  m.rows = args->rows;
+  m.splits = args->parts;
+  m.protocol = MODE_LSE;
+  return status_from_cuda(launch_merge(m, args->head_dim, reinterpret_cast<cudaStream_t>(stream)),
+                          "lse merge");
 }
 
 extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) {

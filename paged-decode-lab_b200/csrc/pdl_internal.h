@@ -48,13 +48,21 @@ struct PartitionParams {
   uint32_t *fault;          // per-device fault word
 };
 
+// Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],
+// weights at lse/maxima/denoms[r*w_row_stride + p*w_part_stride].
 struct MergeParams {
   const float *partial;     // LSE protocol
   const float *lse;
   const float *maxima;      // MLA protocol
   const float *denoms;
   const float *accums;
-  __nv_bfloat16 *out;
+  int64_t row_stride;
+  int64_t part_stride;
+  int64_t w_row_stride;
+  int64_t w_part_stride;
+  __nv_bfloat16 *out;       // BF16 [rows, D], or null
+  float *out_partial;       // FP32 [rows, D] merged partial, or null (LSE protocol)
+  float *out_lse;           // FP32 [rows] merged LSE (-inf if empty), or null
   const int32_t *lengths;   // optional: bound the partitions read per row
   int32_t num_heads;
   int32_t tokens_per_split;

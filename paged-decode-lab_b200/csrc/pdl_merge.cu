@@ -1,18 +1,24 @@
-// pdl_merge.cu -- stable merge of split-K partitions into the BF16 output.
+// pdl_merge.cu -- stable merge of split-K partitions.
 //
 // One warp per (row, query head); lane l owns D/32 contiguous FP32 columns,
 // so each partition row is read with one coalesced vector load per lane.
+// Partition p of row r is read at  rows_src[r * row_stride + p * part_stride]
+// and its weight at  weights_src[r * w_row_stride + p * w_part_stride], so
+// the same kernel merges the split workspace ([B,Hq,S,D], S contiguous) and
+// the rank-major buffer an all-gather produces ([N][B*Hq][D]).
 //
 // LSE protocol (reference src/paged_decode/matched_splitkv.py:101-127):
 //   M = max_p lse_p (an all -inf row uses 0); total = sum_p exp(lse_p - M);
 //   logsum = ln(total) + M, or +inf when total = 0;
 //   out = sum_p exp(lse_p - logsum) * partial_p.
+// Optionally the merged row is stored as an FP32 partial plus its LSE
+// (logsum, or -inf for an empty row), so a merge can feed another merge.
 // MLA protocol (reference src/paged_decode/kernels.py:83-100):
 //   M = max_p m_p (-inf -> 0); f_p = exp(m_p - M);
 //   out = sum_p f_p * acc_p / (sum_p f_p * l_p, or 1 when that is 0).
-// When the caller passes `lengths`, only the ceil(len / tokens_per_split)
-// live partitions of a row are read (the others hold no tokens and their
-// weights are exactly 0), so empty partitions need not be stored at all.
+// When `lengths` is given, only the ceil(len / tokens_per_split) live
+// partitions of a row are read (the others hold no tokens and their weights
+// are exactly 0), so empty partitions need not be stored at all.
 #include "pdl_device.cuh"
 
 namespace pdl {
@@ -31,6 +37,17 @@ __device__ __forceinline__ void load_cols(const float *src, float (&v)[E]) {
       const float4 a = *reinterpret_cast<const float4 *>(src + i);
       v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
     }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void store_cols(float *dst, const float (&v)[E]) {
+  if constexpr (E == 2) {
+    *reinterpret_cast<float2 *>(dst) = make_float2(v[0], v[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; i += 4)
+      *reinterpret_cast<float4 *>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
   }
 }
 
@@ -58,50 +75,55 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
     const int len = __ldg(p.lengths + row / p.num_heads);
     live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
   }
-  const int64_t base = (int64_t)row * p.splits;
-  const float *weights_src = p.protocol == MODE_LSE ? p.lse : p.maxima;
+  const bool lse_protocol = p.protocol == MODE_LSE;
+  const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
+  const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride;
 
   float mx = -INFINITY;
-  for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldg(weights_src + base + s));
+  for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldg(w_src + s * p.w_part_stride));
   mx = warp_max(mx);
   if (mx == -INFINITY) mx = 0.f;
 
-  float shift = mx;  // exponent subtracted from every weight
-  float scale = 1.f; // final multiplier
-  if (p.protocol == MODE_LSE) {
-    float tot = 0.f;
-    for (int s = lane; s < live; s += 32) tot += expf(__ldg(p.lse + base + s) - mx);
+  float shift = mx;   // exponent subtracted from every weight
+  float scale = 1.f;  // final multiplier
+  float tot = 0.f;
+  if (lse_protocol) {
+    for (int s = lane; s < live; s += 32) tot += expf(__ldg(w_src + s * p.w_part_stride) - mx);
     tot = warp_sum(tot);
     shift = tot > 0.f ? logf(tot) + mx : INFINITY;
   } else {
-    float tot = 0.f;
+    const float *l_src = p.denoms + (int64_t)row * p.w_row_stride;
     for (int s = lane; s < live; s += 32)
-      tot += __ldg(p.denoms + base + s) * expf(__ldg(p.maxima + base + s) - mx);
+      tot += __ldg(l_src + s * p.w_part_stride) * expf(__ldg(w_src + s * p.w_part_stride) - mx);
     tot = warp_sum(tot);
     scale = 1.f / (tot > 0.f ? tot : 1.f);
   }
 
-  const float *rows_src = p.protocol == MODE_LSE ? p.partial : p.accums;
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
   for (int s0 = 0; s0 < live; s0 += 32) {
-    const float wl = (s0 + lane < live) ? expf(__ldg(weights_src + base + s0 + lane) - shift) : 0.f;
+    const float wl = (s0 + lane < live) ? expf(__ldg(w_src + (s0 + lane) * p.w_part_stride) - shift)
+                                        : 0.f;
     const int n = min(32, live - s0);
     for (int k = 0; k < n; ++k) {
       const float wk = __shfl_sync(FULL_MASK, wl, k);
       float v[E];
-      load_cols<E>(rows_src + (base + s0 + k) * D + lane * E, v);
+      load_cols<E>(r_src + (int64_t)(s0 + k) * p.part_stride + lane * E, v);
 #pragma unroll
       for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[e], acc[e]);
     }
   }
-  __nv_bfloat16 *dst = p.out + (int64_t)row * D + lane * E;
 #pragma unroll
-  for (int e = 0; e < E; e += 2) {
-    *reinterpret_cast<__nv_bfloat162 *>(dst + e) =
-        __floats2bfloat162_rn(acc[e] * scale, acc[e + 1] * scale);
+  for (int e = 0; e < E; ++e) acc[e] *= scale;
+  if (p.out != nullptr) {
+    __nv_bfloat16 *dst = p.out + (int64_t)row * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 2)
+      *reinterpret_cast<__nv_bfloat162 *>(dst + e) = __floats2bfloat162_rn(acc[e], acc[e + 1]);
   }
+  if (p.out_partial != nullptr) store_cols<E>(p.out_partial + (int64_t)row * D + lane * E, acc);
+  if (p.out_lse != nullptr && lane == 0) p.out_lse[row] = tot > 0.f ? shift : -INFINITY;
 }
 
 }  // namespace

@@ -21,9 +21,9 @@ KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
 FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE = 1, 2
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
-SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_paged_decode", "pdl_paged_decode_static_scratch",
-           "pdl_splitkv_plan", "pdl_spec_geometry", "pdl_status_string", "pdl_last_error",
-           "pdl_abi_version", "pdl_read_fault")
+SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode",
+           "pdl_paged_decode_static_scratch", "pdl_splitkv_plan", "pdl_spec_geometry",
+           "pdl_status_string", "pdl_last_error", "pdl_abi_version", "pdl_read_fault")
 STATIC_SCRATCH_BYTES = 4 << 20
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
@@ -51,6 +51,13 @@ class PdlDecodeArgs(ctypes.Structure):
                 ("lse", _vp), ("maxima", _vp), ("denoms", _vp), ("accums", _vp)]
 
 
+class PdlMergeArgs(ctypes.Structure):
+    _fields_ = [("partial", _vp), ("lse", _vp), ("row_stride", _i64), ("part_stride", _i64),
+                ("lse_row_stride", _i64), ("lse_part_stride", _i64), ("rows", _i32),
+                ("parts", _i32), ("head_dim", _i32), ("out", _vp), ("out_partial", _vp),
+                ("out_lse", _vp)]
+
+
 _LIB = None
 
 
@@ -70,6 +77,8 @@ def load():
         fn = getattr(lib, name)
         fn.argtypes = [args_p, ctypes.c_size_t]  # stream handle as an integer
         fn.restype = ctypes.c_int
+    lib.pdl_lse_merge.argtypes = [ctypes.POINTER(PdlMergeArgs), ctypes.c_size_t]
+    lib.pdl_lse_merge.restype = ctypes.c_int
     lib.pdl_splitkv_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, _i32, ctypes.POINTER(PdlPlan)]
     lib.pdl_splitkv_plan.restype = ctypes.c_int
     lib.pdl_spec_geometry.argtypes = [ctypes.POINTER(PdlSpec), ctypes.POINTER(_i32),

@@ -128,6 +128,31 @@ def paged_decode_static_scratch(args, device):
     _call("pdl_paged_decode_static_scratch", args, device)
 
 
+def merge_args(partial, lse, *, rows, parts, head_dim, row_stride, part_stride, lse_row_stride,
+               lse_part_stride, out=None, out_partial=None, out_lse=None):
+    """Fill a ``PdlMergeArgs`` (strides in floats; tensors give base addresses)."""
+    m = _lib.PdlMergeArgs()
+    m.partial = partial.data_ptr()
+    m.lse = lse.data_ptr()
+    m.row_stride, m.part_stride = int(row_stride), int(part_stride)
+    m.lse_row_stride, m.lse_part_stride = int(lse_row_stride), int(lse_part_stride)
+    m.rows, m.parts, m.head_dim = int(rows), int(parts), int(head_dim)
+    m.out = _addr(out)
+    m.out_partial = _addr(out_partial)
+    m.out_lse = _addr(out_lse)
+    return m
+
+
+def lse_merge(margs, device):
+    """Strided LSE merge (``pdl_lse_merge``)."""
+    fn = _lib.load().pdl_lse_merge
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    with torch.cuda.device(index):
+        status = fn(ctypes.byref(margs), torch.cuda.current_stream().cuda_stream)
+    if status != _lib.PDL_OK:
+        raise RuntimeError(f"pdl_lse_merge failed: {_lib.status_text(status)}")
+
+
 def read_fault(clear=False):
     """Device-side fault word (bounded waits that gave up); synchronises."""
     return _lib.read_fault(clear)
