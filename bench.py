@@ -65,7 +65,63 @@ def parse_args():
     ap.add_argument("--window-seconds", type=float, default=0.5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="partition-kernel GB/s for every (head_dim, group, kernel) at ~1 GB of "
+                         "KV (one JSON line per point; not the contract line)")
     return ap.parse_args()
+
+
+def sweep(reps=20):
+    """Partition kernel alone, graph-timed, ctx 4096, Hkv 8, ~1 GB of KV per launch."""
+    import torch
+    from paged_decode import ops
+    for dim in (64, 128, 256):
+        for group in (1, 2, 4, 8, 16):
+            for kernel in ("simt", "mma"):
+                ctx, hkv = 4096, 8
+                batch = max(1, int(1.0e9 // (ctx * hkv * dim * 4)))
+                width, hq = ctx // 256, hkv * group
+                gen = torch.Generator(device="cuda").manual_seed(0)
+                table = torch.randperm(batch * width, generator=gen, device="cuda")
+                table = table.view(batch, width).to(torch.int32)
+                k = torch.randn(batch * width, 256, hkv, dim, generator=gen,
+                                device="cuda").to(torch.bfloat16)
+                v = torch.randn_like(k)
+                q = torch.randn(batch, hq, dim, generator=gen, device="cuda").to(torch.bfloat16)
+                lens = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+                splits = 4 if batch * hkv < 600 else 1
+                partial = torch.empty(batch, hq, splits, dim, device="cuda")
+                lse = torch.empty(batch, hq, splits, device="cuda")
+                a = ops.decode_args(q, k, v, table, lens, scale=dim ** -0.5,
+                                    tokens_per_split=ctx // splits, splits=splits,
+                                    protocol=ops.PROTOCOL_LSE, kernel=kernel, partial=partial,
+                                    lse=lse)
+                for _ in range(3):
+                    ops.partition(a, q.device)
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    ops.partition(a, q.device)
+                torch.cuda.current_stream().wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(reps):
+                        ops.partition(a, q.device)
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (2 * reps)
+                kv = batch * ctx * hkv * dim * 4
+                print(json.dumps(dict(head_dim=dim, group=group, kernel=kernel, batch=batch,
+                                      splits=splits, us=round(us, 2),
+                                      gbs=round(kv / us / 1e3, 1))), flush=True)
+                del graph, k, v
+                torch.cuda.empty_cache()
 
 
 def config_splits(name, args):
@@ -211,6 +267,9 @@ def main():
         if rank == 0:
             print(json.dumps(reference_line(args)), flush=True)
         return 0
+    if args.sweep:
+        sweep()
+        return 0
 
     # CPU baseline first (rank 0, N = 1): its spawn pool starts before any CUDA work.
     cpu = None
@@ -346,7 +405,7 @@ def main():
     peak, peak_src = measured_peak()
     achieved = local_bytes / (part_ms / 1e3) / 1e9
     group = first.spec.num_heads // first.spec.num_kv_heads
-    kernel_name = "mma" if (args.kernel == "mma" or (args.kernel == "auto" and group >= 8)) \
+    kernel_name = "mma" if (args.kernel == "mma" or (args.kernel == "auto" and group >= 3)) \
         else "simt"
     traffic, traffic_src = committed_traffic(args.config, kernel_name)
 

@@ -57,8 +57,9 @@ typedef enum PdlProtocol {
   PDL_PROTOCOL_MLA = 1
 } PdlProtocol;
 
-/* Which partition kernel runs. AUTO picks the tensor-core kernel when a KV
- * head serves >= 8 query heads and the CUDA-core kernel otherwise. */
+/* Which partition kernel runs. AUTO picks the CUDA-core kernel when a KV head
+ * serves 1 or 2 query heads and the tensor-core kernel from 3 (measured:
+ * the CUDA-core kernel turns issue-bound at 4 heads per KV head). */
 typedef enum PdlKernel {
   PDL_KERNEL_AUTO = 0,
   PDL_KERNEL_SIMT = 1, /* FP32 CUDA-core kernel, warp-shuffle reductions      */

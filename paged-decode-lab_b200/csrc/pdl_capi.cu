@@ -149,12 +149,16 @@ bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 bool valid_dim(int d) { return d == 64 || d == 128 || d == 256; }
 
-// Which partition kernel serves this launch.
+// Which partition kernel serves this launch.  Measured on B200 at ~1 GB of
+// KV: the CUDA-core kernel is at or above the tensor-core one for 1 and 2
+// query heads per KV head and becomes issue-bound from 4 (ncu: 54% issue
+// active, 39% DRAM throughput at D=256), where the tensor-core kernel stays
+// DRAM-bound; so AUTO switches at 3.
 int choose_kernel(const PdlDecodeArgs &a) {
   const int group = a.num_heads / a.num_kv_heads;
   if (a.kernel == PDL_KERNEL_SIMT) return PDL_KERNEL_SIMT;
   if (a.kernel == PDL_KERNEL_MMA) return PDL_KERNEL_MMA;
-  return group >= 8 ? PDL_KERNEL_MMA : PDL_KERNEL_SIMT;
+  return group >= 3 ? PDL_KERNEL_MMA : PDL_KERNEL_SIMT;
 }
 
 // Checks shared by every launch entry point; mirrors the tensor contract of

@@ -44,8 +44,8 @@ def allocate_matched_resources(spec, device, *, num_splits=0):
 def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="auto"):
     """Partition + LSE merge for the fixed plan; returns ``resources.out``.
 
-    ``kernel`` picks the partition kernel: "auto" (tensor cores when a KV
-    head serves >= 8 query heads, CUDA cores otherwise), "simt" or "mma".
+    ``kernel`` picks the partition kernel: "auto" (CUDA cores when a KV head
+    serves 1 or 2 query heads, tensor cores from 3), "simt" or "mma".
     """
     scale = q.shape[-1] ** -.5 if scale is None else float(scale)
     cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
