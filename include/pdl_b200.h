@@ -29,7 +29,7 @@ extern "C" {
 
 typedef struct CUstream_st *pdl_stream_t; /* same handle as cudaStream_t */
 
-#define PDL_ABI_VERSION 1
+#define PDL_ABI_VERSION 2
 #define PDL_PAGE_SIZE 256
 
 typedef enum PdlStatus {
@@ -73,7 +73,17 @@ typedef enum PdlFlags {
   PDL_FLAG_SKIP_EMPTY = 1,
   /* With splits == 1, pdl_paged_decode writes the output directly from the
    * partition kernel and leaves the workspace untouched. */
-  PDL_FLAG_DIRECT_SINGLE = 2
+  PDL_FLAG_DIRECT_SINGLE = 2,
+  /* Lets pdl_paged_decode run ONE kernel: the CTA that finishes the last
+   * partition of a (row, KV head) merges that group's partitions itself.
+   * Used when the launch is short (at most 2 work items per CTA slot) and a
+   * group's partitions are small (splits * heads * head_dim * 4 <= 32 KB),
+   * where the second launch is a large share of the step; otherwise the
+   * library keeps the two-kernel path (the merge then starts early through
+   * programmatic dependent launch).  Needs `counters`, zero-initialised once; the
+   * kernel leaves it zeroed.  The workspace is still written and the output
+   * is bit-identical to the two-kernel path. */
+  PDL_FLAG_FUSED_MERGE = 4
 } PdlFlags;
 
 /* Geometry contract; mirrors DecodeSpec (reference src/paged_decode/spec.py:11-30). */
@@ -125,6 +135,7 @@ typedef struct PdlDecodeArgs {
   float *maxima;              /* MLA protocol: [batch, num_heads, splits]          */
   float *denoms;              /*               [batch, num_heads, splits]          */
   float *accums;              /*               [batch, num_heads, splits, head_dim] */
+  int32_t *counters;          /* PDL_FLAG_FUSED_MERGE: int32 [batch * num_heads], zeroed */
 } PdlDecodeArgs;
 
 /* Partition kernel: per (row, KV head, partition) online softmax over the

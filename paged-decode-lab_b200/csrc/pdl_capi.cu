@@ -213,8 +213,10 @@ int status_from_cuda(cudaError_t e, const char *where) {
   return e == cudaSuccess ? PDL_OK : cuda_fail(where, e);
 }
 
-// Launch the partition kernel in `mode` (MODE_LSE / MODE_MLA / MODE_DIRECT).
-int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
+// Launch the partition kernel in `mode` (MODE_LSE / MODE_MLA / MODE_DIRECT);
+// `fused` lets it merge finished groups itself (PDL_FLAG_FUSED_MERGE).
+int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream, bool fused = false,
+                  bool *did_fuse = nullptr) {
   DeviceState *dev = nullptr;
   int st = current_device_state(&dev);
   if (st != PDL_OK) return st;
@@ -273,6 +275,16 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   p.denoms = a->denoms;
   p.accums = a->accums;
   p.fault = dev->fault;
+  // The fused merge pays off when the launch is short (at most two items per
+  // CTA slot), where a second kernel launch is a large share of the step; on
+  // long launches the per-item counting costs more than the launch it saves.
+  // Only small merges are fused: the merging CTA pulls a whole group's
+  // partitions through one SM, while the separate merge kernel spreads them.
+  const int64_t group_bytes = (int64_t)a->splits * per_cta * a->head_dim * 4;
+  const bool fuse = fused && mode != MODE_DIRECT && items <= 4LL * dev->sm_count &&
+                    group_bytes <= 32 * 1024;
+  p.counters = fuse ? a->counters : nullptr;
+  if (did_fuse) *did_fuse = fuse;
   const cudaError_t e = which == PDL_KERNEL_SIMT ? launch_partition_simt(L, stream)
                                                  : launch_partition_mma(L, stream);
   return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
@@ -287,7 +299,9 @@ int run_merge(const PdlDecodeArgs *a, cudaStream_t stream) {
   m.denoms = a->denoms;
   m.accums = a->accums;
   m.out = static_cast<__nv_bfloat16 *>(a->out);
-  m.lengths = (a->flags & PDL_FLAG_SKIP_EMPTY) ? a->lengths : nullptr;
+  // Partitions past ceil(len / tokens_per_split) are empty and weigh exactly
+  // 0, so the merge reads only the live ones whenever lengths are known.
+  m.lengths = a->lengths;
   m.num_heads = a->num_heads;
   m.tokens_per_split = a->tokens_per_split > 0 ? a->tokens_per_split : (1 << 30);
   m.rows = a->batch * a->num_heads;
@@ -467,7 +481,16 @@ extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) 
   if (direct) return run_partition(args, MODE_DIRECT, s);
   st = validate_workspace(args);
   if (st != PDL_OK) return st;
-  st = run_partition(args, args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA, s);
+  const int mode = args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA;
+  if (args->flags & PDL_FLAG_FUSED_MERGE) {
+    if (!args->counters) return fail(PDL_ERR_WORKSPACE, "pdl_paged_decode", "fused merge needs counters");
+    if (!aligned(args->counters, 4)) return PDL_ERR_ALIGNMENT;
+    bool fused = false;
+    st = run_partition(args, mode, s, true, &fused);
+    if (st != PDL_OK || fused) return st;
+    return run_merge(args, s);
+  }
+  st = run_partition(args, mode, s);
   if (st != PDL_OK) return st;
   return run_merge(args, s);
 }

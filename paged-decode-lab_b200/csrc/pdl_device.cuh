@@ -153,6 +153,19 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched after this one with
+// programmatic stream serialization may start once every CTA here has
+// executed launch_dependents (or exited); it must call grid_dependency_wait
+// before touching this kernel's outputs, which returns once this kernel has
+// completed and its memory operations are visible.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 constexpr float LN2 = 0.6931471805599453f;
 
 }  // namespace pdl

@@ -46,6 +46,7 @@ struct PartitionParams {
   float *denoms;
   float *accums;
   uint32_t *fault;          // per-device fault word
+  int32_t *counters;        // fused merge: finished items per (row, KV head, sub-group), or null
 };
 
 // Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],

@@ -1,7 +1,12 @@
 // pdl_merge.cu -- stable merge of split-K partitions.
 //
-// One warp per (row, query head); lane l owns D/32 contiguous FP32 columns,
-// so each partition row is read with one coalesced vector load per lane.
+// One warp per (row, query head, column slice of at most 128 floats); lane l
+// owns 4 (or D/32 for D = 64) contiguous FP32 columns of the slice, so each
+// partition row is read with one coalesced vector load per lane, and rows of
+// eight partitions are in flight at once.  The kernel is launched with
+// programmatic stream serialization: its CTAs may be scheduled while the
+// partition kernel still runs and wait (griddepcontrol.wait) for it to
+// complete before reading anything.
 // Partition p of row r is read at  rows_src[r * row_stride + p * part_stride]
 // and its weight at  weights_src[r * w_row_stride + p * w_part_stride], so
 // the same kernel merges the split workspace ([B,Hq,S,D], S contiguous) and
@@ -66,9 +71,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int D>
 __global__ void __launch_bounds__(32 * MERGE_WARPS)
     merge_kernel(const MergeParams p) {
-  constexpr int E = D / 32;
+  constexpr int CW = D < 128 ? D : 128;  // columns per warp
+  constexpr int SLICES = D / CW;
+  constexpr int E = CW / 32;
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
+  const int unit = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
+  const int row = unit / SLICES, col0 = (unit % SLICES) * CW;
+  grid_dependency_wait();
   if (row >= p.rows) return;
   int live = p.splits;
   if (p.lengths != nullptr) {
@@ -77,7 +86,7 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   }
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
-  const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride;
+  const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;
 
   float mx = -INFINITY;
   for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldg(w_src + s * p.w_part_stride));
@@ -106,38 +115,65 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
     const float wl = (s0 + lane < live) ? expf(__ldg(w_src + (s0 + lane) * p.w_part_stride) - shift)
                                         : 0.f;
     const int n = min(32, live - s0);
-    for (int k = 0; k < n; ++k) {
-      const float wk = __shfl_sync(FULL_MASK, wl, k);
-      float v[E];
-      load_cols<E>(r_src + (int64_t)(s0 + k) * p.part_stride + lane * E, v);
+    // Rows of up to 8 partitions are loaded before any is consumed, so the
+    // memory round trips overlap instead of serialising per partition.
+    for (int k0 = 0; k0 < n; k0 += 8) {
+      float v[8][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[e], acc[e]);
+      for (int j = 0; j < 8; ++j)
+        load_cols<E>(r_src + (int64_t)(s0 + min(k0 + j, n - 1)) * p.part_stride + lane * E, v[j]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float wk = __shfl_sync(FULL_MASK, wl, min(k0 + j, 31));
+        if (k0 + j < n) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[j][e], acc[e]);
+        }
+      }
     }
   }
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] *= scale;
   if (p.out != nullptr) {
-    __nv_bfloat16 *dst = p.out + (int64_t)row * D + lane * E;
+    __nv_bfloat16 *dst = p.out + (int64_t)row * D + col0 + lane * E;
 #pragma unroll
     for (int e = 0; e < E; e += 2)
       *reinterpret_cast<__nv_bfloat162 *>(dst + e) = __floats2bfloat162_rn(acc[e], acc[e + 1]);
   }
-  if (p.out_partial != nullptr) store_cols<E>(p.out_partial + (int64_t)row * D + lane * E, acc);
-  if (p.out_lse != nullptr && lane == 0) p.out_lse[row] = tot > 0.f ? shift : -INFINITY;
+  if (p.out_partial != nullptr)
+    store_cols<E>(p.out_partial + (int64_t)row * D + col0 + lane * E, acc);
+  if (p.out_lse != nullptr && lane == 0 && col0 == 0)
+    p.out_lse[row] = tot > 0.f ? shift : -INFINITY;
+}
+
+template <int D>
+cudaError_t launch_merge_t(const MergeParams &params, cudaStream_t stream) {
+  constexpr int SLICES = D / (D < 128 ? D : 128);
+  const int64_t units = (int64_t)params.rows * SLICES;
+  const int grid = (int)((units + MERGE_WARPS - 1) / MERGE_WARPS);
+  if (grid <= 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(32 * MERGE_WARPS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_kernel<D>, params);
 }
 
 }  // namespace
 
 cudaError_t launch_merge(const MergeParams &params, int head_dim, cudaStream_t stream) {
-  const int grid = (params.rows + MERGE_WARPS - 1) / MERGE_WARPS;
-  if (grid <= 0) return cudaSuccess;
   switch (head_dim) {
-    case 64: merge_kernel<64><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
-    case 128: merge_kernel<128><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
-    case 256: merge_kernel<256><<<grid, 32 * MERGE_WARPS, 0, stream>>>(params); break;
+    case 64: return launch_merge_t<64>(params, stream);
+    case 128: return launch_merge_t<128>(params, stream);
+    case 256: return launch_merge_t<256>(params, stream);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace pdl

@@ -109,8 +109,12 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFFSET);
   uint64_t *empty = full + NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + NS);
+  volatile int *merge_flag = abort_flag + 1;
   if (!smem_base_aligned(smem, p.fault)) return;
 
+  // The merge kernel that follows may be scheduled now; it waits for this
+  // grid to complete before reading the workspace.
+  allow_dependent_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -147,6 +151,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     if (rg.start >= rg.stop) {
       if (p.write_empty || p.mode == MODE_DIRECT)
         store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
+      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
       continue;
     }
 
@@ -325,6 +330,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     named_barrier(1, NC * 32);
     combine_and_store<D, GC, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
+    finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
   }
 }
 

@@ -184,6 +184,103 @@ __device__ void combine_and_store(const PartitionParams &p, const Item &w, int h
   }
 }
 
+// Fused merge of one (row, KV head, sub-group): the consumer warps of the CTA
+// that finished the group's last partition combine its partitions (stored by
+// any CTA of this launch, so read through L2 with ld.global.cg) into the BF16
+// output, with the arithmetic of merge_kernel (pdl_merge.cu).  Warp w takes
+// heads w, w+NC, ...; lane l owns D/32 contiguous columns.
+template <int D, int NC>
+__device__ void merge_group(const PartitionParams &p, const Item &w, int h0, int rows, int live,
+                            int cw, int lane) {
+  constexpr int E = D / 32;
+  for (int g = cw; g < rows; g += NC) {
+    const int64_t row = (int64_t)w.b * p.num_heads + h0 + g;
+    const int64_t base = row * p.splits;
+    const bool lse_protocol = p.mode == MODE_LSE;
+    const float *wsrc = (lse_protocol ? p.lse : p.maxima) + base;
+    float mx = -INFINITY;
+    for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldcg(wsrc + s));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
+    if (mx == -INFINITY) mx = 0.f;
+    float tot = 0.f;
+    for (int s = lane; s < live; s += 32) {
+      const float e = expf(__ldcg(wsrc + s) - mx);
+      tot += lse_protocol ? e : e * __ldcg(p.denoms + base + s);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) tot += __shfl_xor_sync(FULL_MASK, tot, o);
+    const float shift = lse_protocol ? (tot > 0.f ? logf(tot) + mx : INFINITY) : mx;
+    const float scale = lse_protocol ? 1.f : 1.f / (tot > 0.f ? tot : 1.f);
+    const float *rsrc = (lse_protocol ? p.partial : p.accums) + base * D + lane * E;
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    for (int s0 = 0; s0 < live; s0 += 32) {
+      const float wl = s0 + lane < live ? expf(__ldcg(wsrc + s0 + lane) - shift) : 0.f;
+      const int n = min(32, live - s0);
+      // Rows of up to 8 partitions are loaded before any is consumed, so the
+      // L2 round trips overlap instead of serialising per partition.
+      for (int k0 = 0; k0 < n; k0 += 8) {
+        float2 v[8][E / 2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float *src = rsrc + (int64_t)(s0 + min(k0 + j, n - 1)) * D;
+#pragma unroll
+          for (int e = 0; e < E; e += 2) v[j][e / 2] = __ldcg(reinterpret_cast<const float2 *>(src + e));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float wk = __shfl_sync(FULL_MASK, wl, min(k0 + j, 31));
+          if (k0 + j < n) {
+#pragma unroll
+            for (int e = 0; e < E; e += 2) {
+              acc[e] = fmaf(wk, v[j][e / 2].x, acc[e]);
+              acc[e + 1] = fmaf(wk, v[j][e / 2].y, acc[e + 1]);
+            }
+          }
+        }
+      }
+    }
+    __nv_bfloat16 *dst = p.out + row * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 2)
+      *reinterpret_cast<__nv_bfloat162 *>(dst + e) =
+          __floats2bfloat162_rn(acc[e] * scale, acc[e + 1] * scale);
+  }
+}
+
+// End of every item (empty or not).  With the fused merge enabled, count the
+// item against its (row, KV head, sub-group); the CTA whose count completes
+// the group's `splits` items merges the group and resets the counter for the
+// next launch.  Release: a CTA barrier orders all consumers' stores before
+// one thread's fence + atomic; acquire: the merging CTA fences after
+// observing the count.
+template <int D, int NC>
+__device__ void finish_item(const PartitionParams &p, const Item &w, int h0, int rows, int cw,
+                            int lane, volatile int *merge_flag) {
+  if (p.counters == nullptr || p.mode == MODE_DIRECT) return;
+  named_barrier(1, NC * 32);  // every consumer's partition stores precede the fence below
+  if (cw == 0 && lane == 0) {
+    const int64_t g = ((int64_t)w.b * p.num_kv_heads + w.kvh) * p.nsub + w.sub;
+    __threadfence();          // release (cumulative over the CTA's stores ordered by the barrier)
+    const int prev = atomicAdd(p.counters + g, 1);
+    const int last = prev == p.splits - 1;
+    if (last) atomicExch(p.counters + g, 0);
+    *merge_flag = last;
+  }
+  named_barrier(1, NC * 32);
+  if (*merge_flag) {
+    __threadfence();
+    // Only the ceil(len / tokens_per_split) live partitions carry weight; the
+    // others are empty (weight exactly 0), so skipping them changes no bit.
+    const int len = min(__ldg(p.lengths + w.b), p.table_width * 256);
+    const int live =
+        min(p.splits, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+    merge_group<D, NC>(p, w, h0, rows, live, cw, lane);
+  }
+}
+
 // Dynamic shared memory one CTA may use so that two CTAs share an SM
 // (228 KB per SM, 1 KB reserved per CTA).
 constexpr int kTwoCtaSmemBytes = 233472 / 2 - 1024;

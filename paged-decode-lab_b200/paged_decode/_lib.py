@@ -8,7 +8,7 @@ import ctypes
 from pathlib import Path
 
 LIBRARY = Path(__file__).with_name("libpdl_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 PDL_OK = 0
 STATUS_NAMES = {
@@ -18,7 +18,7 @@ STATUS_NAMES = {
 }
 PROTOCOL_LSE, PROTOCOL_MLA = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
-FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE = 1, 2
+FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE = 1, 2, 4
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
 SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode",
@@ -48,7 +48,8 @@ class PdlDecodeArgs(ctypes.Structure):
                 ("num_kv_heads", _i32), ("head_dim", _i32), ("scale", _f32),
                 ("tokens_per_split", _i32), ("splits", _i32), ("protocol", _i32),
                 ("kernel", _i32), ("flags", _i32), ("out", _vp), ("partial", _vp),
-                ("lse", _vp), ("maxima", _vp), ("denoms", _vp), ("accums", _vp)]
+                ("lse", _vp), ("maxima", _vp), ("denoms", _vp), ("accums", _vp),
+                ("counters", _vp)]
 
 
 class PdlMergeArgs(ctypes.Structure):

@@ -24,6 +24,9 @@ class MatchedResources:
     out: torch.Tensor
     partials: torch.Tensor
     lse: torch.Tensor
+    # Group counters of the fused partition+merge kernel (zeroed; the kernel
+    # leaves them zeroed).  None selects the two-kernel launch.
+    counters: torch.Tensor | None = None
 
 
 def allocate_matched_resources(spec, device, *, num_splits=0):
@@ -38,7 +41,8 @@ def allocate_matched_resources(spec, device, *, num_splits=0):
         torch.empty((spec.max_batch, spec.num_heads, spec.head_dim), device=device,
                     dtype=torch.bfloat16),
         torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32),
-        torch.empty(shape, device=device, dtype=torch.float32))
+        torch.empty(shape, device=device, dtype=torch.float32),
+        torch.zeros(spec.max_batch * spec.num_heads, device=device, dtype=torch.int32))
 
 
 def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="auto"):
@@ -50,7 +54,8 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
     scale = q.shape[-1] ** -.5 if scale is None else float(scale)
     cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
     key = ((kernel, scale, q.device) + ops.tensor_key(q, k, v, tables, lengths)
-           + ops.buffers_key(resources.out, resources.partials, resources.lse))
+           + ops.buffers_key(resources.out, resources.partials, resources.lse,
+                             resources.counters))
     args = cache.get(key)
     if args is not None:
         ops.paged_decode(args, q.device)
@@ -70,7 +75,9 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
     args = ops.decode_args(q, k, v, tables, lengths, scale=scale,
                            tokens_per_split=plan.tokens_per_split, splits=plan.splits,
                            protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
-                           partial=resources.partials, lse=resources.lse)
+                           partial=resources.partials, lse=resources.lse,
+                           counters=resources.counters,
+                           flags=0 if resources.counters is None else ops.FLAG_FUSED_MERGE)
     ops.paged_decode(args, q.device)
     cache.put(key, args)
     return resources.out

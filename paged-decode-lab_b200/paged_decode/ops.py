@@ -19,6 +19,7 @@ KERNEL_SIMT = _lib.KERNEL_SIMT
 KERNEL_MMA = _lib.KERNEL_MMA
 FLAG_SKIP_EMPTY = _lib.FLAG_SKIP_EMPTY
 FLAG_DIRECT_SINGLE = _lib.FLAG_DIRECT_SINGLE
+FLAG_FUSED_MERGE = _lib.FLAG_FUSED_MERGE
 
 _KERNELS = {"auto": KERNEL_AUTO, "simt": KERNEL_SIMT, "mma": KERNEL_MMA}
 
@@ -29,7 +30,7 @@ def _addr(t):
 
 def decode_args(q, k, v, tables, lengths, *, scale, tokens_per_split=0, splits=1,
                 protocol=PROTOCOL_LSE, kernel="auto", flags=0, out=None, partial=None,
-                lse=None, maxima=None, denoms=None, accums=None):
+                lse=None, maxima=None, denoms=None, accums=None, counters=None):
     """Fill a ``PdlDecodeArgs`` from tensors (element strides, raw addresses)."""
     a = _lib.PdlDecodeArgs()
     a.q = q.data_ptr()
@@ -58,6 +59,7 @@ def decode_args(q, k, v, tables, lengths, *, scale, tokens_per_split=0, splits=1
     a.maxima = _addr(maxima)
     a.denoms = _addr(denoms)
     a.accums = _addr(accums)
+    a.counters = _addr(counters)
     return a
 
 

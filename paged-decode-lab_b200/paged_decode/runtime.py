@@ -34,6 +34,9 @@ class Resources:
     maxima: torch.Tensor | None = None
     denoms: torch.Tensor | None = None
     accums: torch.Tensor | None = None
+    # Group counters of the fused partition+merge kernel (zeroed, split
+    # backends only; the kernel leaves them zeroed).
+    counters: torch.Tensor | None = None
 
 
 def allocate_resources(spec, device, backend="triton_splitk"):
@@ -52,6 +55,8 @@ def allocate_resources(spec, device, backend="triton_splitk"):
         result.maxima = torch.empty(shape, device=device, dtype=torch.float32)
         result.denoms = torch.empty(shape, device=device, dtype=torch.float32)
         result.accums = torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32)
+        result.counters = torch.zeros(spec.max_batch * spec.num_heads, device=device,
+                                      dtype=torch.int32)
     return result
 
 
@@ -135,7 +140,8 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
     scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
     cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
     key = ((backend, scale, q.device) + ops.tensor_key(q, k, v, tables, lengths)
-           + ops.buffers_key(resources.out, resources.maxima, resources.denoms, resources.accums))
+           + ops.buffers_key(resources.out, resources.maxima, resources.denoms, resources.accums,
+                             resources.counters))
     args = cache.get(key)
     if args is not None:
         ops.paged_decode(args, q.device)
@@ -162,7 +168,8 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
                                tokens_per_split=PARTITION_SIZE, splits=spec.partitions,
                                protocol=ops.PROTOCOL_MLA, kernel=kernel, out=resources.out,
                                maxima=resources.maxima, denoms=resources.denoms,
-                               accums=resources.accums)
+                               accums=resources.accums, counters=resources.counters,
+                               flags=0 if resources.counters is None else ops.FLAG_FUSED_MERGE)
     else:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)

@@ -157,3 +157,31 @@ def test_split_layout_invariance(kernel):
     assert_out_close(a, ref)
     assert_out_close(b, ref)
     assert (a.float() - b.float()).abs().max().item() <= 2 ** -7
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("protocol", ["lse", "mla"])
+@pytest.mark.parametrize("skip_empty", [False, True])
+def test_fused_merge_equals_two_kernel_path(kernel, protocol, skip_empty):
+    """One kernel (last CTA of a group merges) == partition + merge kernels, bit for bit."""
+    case = cases.make_case([3000, 0, 1, 4096, 257], 8, 2, 128, seed=12, capacity=4096)
+    q, k, v, table, lens = device_case(case)
+    counters = torch.zeros(5 * 8, dtype=torch.int32, device="cuda")
+    outs = []
+    for fused in (False, True):
+        out = torch.empty(5, 8, 128, dtype=torch.bfloat16, device="cuda")
+        ws = dict(partial=torch.empty(5, 8, 8, 128, device="cuda"),
+                  lse=torch.empty(5, 8, 8, device="cuda")) if protocol == "lse" else dict(
+            maxima=torch.empty(5, 8, 8, device="cuda"), denoms=torch.empty(5, 8, 8, device="cuda"),
+            accums=torch.empty(5, 8, 8, 128, device="cuda"))
+        flags = (ops.FLAG_SKIP_EMPTY if skip_empty else 0) | (ops.FLAG_FUSED_MERGE if fused else 0)
+        args = ops.decode_args(q, k, v, table, lens, scale=0.09, tokens_per_split=512, splits=8,
+                               protocol=ops.PROTOCOL_LSE if protocol == "lse" else ops.PROTOCOL_MLA,
+                               kernel=kernel, flags=flags, out=out, counters=counters, **ws)
+        for _ in range(2):  # the second launch reuses the counters the first left zeroed
+            ops.paged_decode(args, q.device)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert not counters.any()
+    assert_out_close(outs[1], oracle.dense_reference(*case.arrays(), scale=0.09))
