@@ -210,6 +210,39 @@ int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream);
  * that overlap on the GPU race.  Nothing is allocated. */
 int pdl_paged_decode_static_scratch(const PdlDecodeArgs *args, pdl_stream_t stream);
 
+/* New K/V rows to append to the paged cache (element strides). */
+typedef struct PdlAppendArgs {
+  const void *key;            /* bf16 [n_tokens, num_kv_heads, head_dim], head_dim contiguous */
+  const void *value;
+  int64_t key_stride_token;
+  int64_t key_stride_head;
+  int64_t value_stride_token;
+  int64_t value_stride_head;
+  void *k_cache;              /* bf16 [num_pages, 256, num_kv_heads, head_dim] contiguous */
+  void *v_cache;
+  int64_t num_pages;
+  int32_t n_tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  /* Slot mode: physical slot (page * 256 + offset) per token; -1 skips it. */
+  const int32_t *slot_mapping;
+  /* Table mode (slot_mapping == NULL): token b is row b's next position. */
+  const int32_t *block_table; /* [n_tokens, table_width], row stride below */
+  int64_t table_stride;
+  int32_t table_width;
+  int32_t *lengths;           /* [n_tokens]; read as the write position */
+  int32_t increment_lengths;  /* 1: lengths[b] += 1 after its slot is resolved */
+} PdlAppendArgs;
+
+/* Copy each new token's K and V rows into its cache slot.  Slot mode
+ * replaces store_kvcache (reference overlays/nano-vllm/nanovllm/layers/
+ * attention.py:10-40); table mode replaces the paged write of
+ * PagedHybridCache.update (reference src/paged_decode/hybrid.py:63-72) for a
+ * decode position, with the length update done on the device so a decode
+ * loop can be captured in a CUDA graph.  Slots outside the pool and rows
+ * whose table is full are skipped. */
+int pdl_append_kv(const PdlAppendArgs *args, pdl_stream_t stream);
+
 /* Static plan for `spec` on `sm_count` SMs; num_splits 0 = heuristic.
  * Replaces make_splitkv_plan (reference src/paged_decode/splitkv_plan.py:26-56). */
 int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,

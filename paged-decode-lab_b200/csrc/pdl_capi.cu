@@ -495,6 +495,46 @@ extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) 
   return run_merge(args, s);
 }
 
+extern "C" int pdl_append_kv(const PdlAppendArgs *args, pdl_stream_t stream) {
+  if (args == nullptr || !args->key || !args->value || !args->k_cache || !args->v_cache)
+    return PDL_ERR_NULL;
+  if (!valid_dim(args->head_dim) || args->num_kv_heads <= 0) return PDL_ERR_GEOMETRY;
+  if (args->n_tokens < 0 || args->num_pages <= 0) return PDL_ERR_SHAPE;
+  if (args->key_stride_head < args->head_dim || args->value_stride_head < args->head_dim)
+    return PDL_ERR_SHAPE;
+  if (!args->slot_mapping) {
+    if (!args->block_table || !args->lengths) return PDL_ERR_NULL;
+    if (args->table_width <= 0 || args->table_stride < args->table_width) return PDL_ERR_SHAPE;
+  }
+  if (!aligned(args->k_cache, 16) || !aligned(args->v_cache, 16)) return PDL_ERR_ALIGNMENT;
+  if (!aligned(args->key, 2) || !aligned(args->value, 2)) return PDL_ERR_ALIGNMENT;
+  AppendParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.key = static_cast<const __nv_bfloat16 *>(args->key);
+  p.value = static_cast<const __nv_bfloat16 *>(args->value);
+  p.key_stride_token = args->key_stride_token;
+  p.key_stride_head = args->key_stride_head;
+  p.value_stride_token = args->value_stride_token;
+  p.value_stride_head = args->value_stride_head;
+  p.k_cache = static_cast<__nv_bfloat16 *>(args->k_cache);
+  p.v_cache = static_cast<__nv_bfloat16 *>(args->v_cache);
+  p.num_pages = args->num_pages;
+  p.n_tokens = args->n_tokens;
+  p.num_kv_heads = args->num_kv_heads;
+  p.head_dim = args->head_dim;
+  p.slot_mapping = args->slot_mapping;
+  p.table = args->block_table;
+  p.table_stride = args->table_stride;
+  p.table_width = args->table_width;
+  p.lengths = args->lengths;
+  p.increment = args->increment_lengths ? 1 : 0;
+  p.key_vec16 = aligned(args->key, 16) && args->key_stride_token % 8 == 0 &&
+                args->key_stride_head % 8 == 0;
+  p.value_vec16 = aligned(args->value, 16) && args->value_stride_token % 8 == 0 &&
+                  args->value_stride_head % 8 == 0;
+  return status_from_cuda(launch_append(p, reinterpret_cast<cudaStream_t>(stream)), "append");
+}
+
 extern "C" int pdl_read_fault(uint32_t *fault, int clear) {
   if (!fault) return PDL_ERR_NULL;
   DeviceState *dev = nullptr;

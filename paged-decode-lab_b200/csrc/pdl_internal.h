@@ -72,6 +72,30 @@ struct MergeParams {
   int32_t protocol;         // MODE_LSE or MODE_MLA
 };
 
+// New K/V rows -> paged cache (pdl_append.cu).
+struct AppendParams {
+  const __nv_bfloat16 *key;
+  const __nv_bfloat16 *value;
+  int64_t key_stride_token, key_stride_head;      // elements
+  int64_t value_stride_token, value_stride_head;  // elements
+  __nv_bfloat16 *k_cache;
+  __nv_bfloat16 *v_cache;
+  int64_t num_pages;
+  int32_t n_tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  const int32_t *slot_mapping;  // slot mode, or null for table mode
+  const int32_t *table;         // table mode
+  int64_t table_stride;
+  int32_t table_width;
+  int32_t *lengths;             // table mode: write position, incremented when `increment`
+  int32_t increment;
+  int32_t key_vec16;            // 16-byte vector copies allowed
+  int32_t value_vec16;
+};
+
+cudaError_t launch_append(const AppendParams &params, cudaStream_t stream);
+
 struct KernelLaunch {
   const CUtensorMap *k_map;
   const CUtensorMap *v_map;

@@ -21,7 +21,7 @@ KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
 FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE = 1, 2, 4
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
-SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode",
+SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode", "pdl_append_kv",
            "pdl_paged_decode_static_scratch", "pdl_splitkv_plan", "pdl_spec_geometry",
            "pdl_status_string", "pdl_last_error", "pdl_abi_version", "pdl_read_fault")
 STATIC_SCRATCH_BYTES = 4 << 20
@@ -52,6 +52,16 @@ class PdlDecodeArgs(ctypes.Structure):
                 ("counters", _vp)]
 
 
+class PdlAppendArgs(ctypes.Structure):
+    _fields_ = [("key", _vp), ("value", _vp), ("key_stride_token", _i64),
+                ("key_stride_head", _i64), ("value_stride_token", _i64),
+                ("value_stride_head", _i64), ("k_cache", _vp), ("v_cache", _vp),
+                ("num_pages", _i64), ("n_tokens", _i32), ("num_kv_heads", _i32),
+                ("head_dim", _i32), ("slot_mapping", _vp), ("block_table", _vp),
+                ("table_stride", _i64), ("table_width", _i32), ("lengths", _vp),
+                ("increment_lengths", _i32)]
+
+
 class PdlMergeArgs(ctypes.Structure):
     _fields_ = [("partial", _vp), ("lse", _vp), ("row_stride", _i64), ("part_stride", _i64),
                 ("lse_row_stride", _i64), ("lse_part_stride", _i64), ("rows", _i32),
@@ -78,6 +88,8 @@ def load():
         fn = getattr(lib, name)
         fn.argtypes = [args_p, ctypes.c_size_t]  # stream handle as an integer
         fn.restype = ctypes.c_int
+    lib.pdl_append_kv.argtypes = [ctypes.POINTER(PdlAppendArgs), ctypes.c_size_t]
+    lib.pdl_append_kv.restype = ctypes.c_int
     lib.pdl_lse_merge.argtypes = [ctypes.POINTER(PdlMergeArgs), ctypes.c_size_t]
     lib.pdl_lse_merge.restype = ctypes.c_int
     lib.pdl_splitkv_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, _i32, ctypes.POINTER(PdlPlan)]

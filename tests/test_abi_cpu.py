@@ -99,7 +99,7 @@ def test_native_geometry_rejects_bad_specs():
 def test_launch_entry_points_reject_null_args_without_a_gpu():
     lib = _lib.load()
     for name in ("pdl_partition", "pdl_merge", "pdl_paged_decode",
-                 "pdl_paged_decode_static_scratch", "pdl_lse_merge"):
+                 "pdl_paged_decode_static_scratch", "pdl_lse_merge", "pdl_append_kv"):
         assert getattr(lib, name)(None, 0) == 1
 
 

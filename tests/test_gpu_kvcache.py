@@ -1,0 +1,109 @@
+"""GPU tests of the paged KV append and of a graph-captured decode loop.
+
+Append parity is bit-exact against a NumPy scatter (byte work).  The loop test
+follows BASELINE config 3's protocol at a reduced size: each step appends one
+token per row at its current length (lengths += 1 on the device) and decodes;
+the whole multi-step loop is captured once in a CUDA graph and replayed.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from gpu_util import assert_out_close, device_case, requires_cuda
+from paged_decode.kvcache import append_decode_kv, store_kvcache
+from paged_decode.matched_splitkv import allocate_matched_resources, matched_decode
+from paged_decode.spec import DecodeSpec
+
+pytestmark = [pytest.mark.gpu, requires_cuda]
+
+
+def bits(t):
+    return t.view(torch.int16).cpu().numpy()
+
+
+@pytest.mark.parametrize("hkv,dim", [(1, 64), (2, 128), (4, 256), (8, 128)])
+def test_store_kvcache_slot_mapping(hkv, dim):
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    pages, n = 6, 40
+    k = torch.randn(pages, 256, hkv, dim, generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn_like(k)
+    # Strided source rows (a slice of a wider buffer) exercise the stride path.
+    wide = torch.randn(n, hkv, dim * 2, generator=gen, device="cuda").to(torch.bfloat16)
+    key, value = wide[:, :, :dim], wide[:, :, dim:]
+    slots = torch.randperm(pages * 256, generator=gen, device="cuda")[:n].to(torch.int32)
+    slots[::7] = -1
+    ek, ev = bits(k).copy(), bits(v).copy()
+    s = slots.cpu().numpy()
+    for i in range(n):
+        if s[i] >= 0:
+            ek[s[i] // 256, s[i] % 256] = bits(key[i])
+            ev[s[i] // 256, s[i] % 256] = bits(value[i])
+    store_kvcache(key, value, k, v, slots)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(k), ek)
+    np.testing.assert_array_equal(bits(v), ev)
+
+
+def test_append_decode_kv_table_mode_and_full_rows():
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    b, hkv, dim, width = 5, 2, 128, 3
+    k = torch.randn(b * width, 256, hkv, dim, generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn_like(k)
+    table = torch.randperm(b * width, generator=gen, device="cuda").view(b, width).to(torch.int32)
+    lens = torch.tensor([0, 255, 256, 767, 768], dtype=torch.int32, device="cuda")  # last is full
+    key = torch.randn(b, hkv, dim, generator=gen, device="cuda").to(torch.bfloat16)
+    value = torch.randn_like(key)
+    ek, ev, t = bits(k).copy(), bits(v).copy(), table.cpu().numpy()
+    for row, n in enumerate(lens.tolist()):
+        if n < width * 256:
+            ek[t[row, n // 256], n % 256] = bits(key[row])
+            ev[t[row, n // 256], n % 256] = bits(value[row])
+    append_decode_kv(key, value, k, v, table, lens)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(k), ek)
+    np.testing.assert_array_equal(bits(v), ev)
+    assert lens.tolist() == [1, 256, 257, 768, 768]
+
+
+def test_graph_captured_decode_loop_with_device_lengths():
+    """Config 3 shape (Hq=16, Hkv=4, D=256, 2% of K channels x8), 4 rows, 24 steps in one graph."""
+    steps, b, hq, hkv, dim, start = 24, 4, 16, 4, 256, 500
+    case = cases.make_case([start] * b, hq, hkv, dim, seed=41, capacity=start + steps)
+    q, k, v, table, lens = device_case(case)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    outlier = torch.ones(hkv * dim, device="cuda")
+    outlier[torch.randperm(hkv * dim, generator=gen, device="cuda")[:round(0.02 * hkv * dim)]] = 8
+    k.copy_((k.float() * outlier.view(1, 1, hkv, dim)).to(torch.bfloat16))
+    new_k = torch.randn(steps, b, hkv, dim, generator=gen, device="cuda").to(torch.bfloat16)
+    new_v = torch.randn_like(new_k)
+    new_q = torch.randn(steps, b, hq, dim, generator=gen, device="cuda").to(torch.bfloat16)
+    res = allocate_matched_resources(DecodeSpec(b, hq, hkv, dim, start + steps), "cuda")
+    outs = torch.empty(steps, b, hq, dim, dtype=torch.bfloat16, device="cuda")
+
+    def loop():
+        for s in range(steps):
+            append_decode_kv(new_k[s], new_v[s], k, v, table, lens)
+            outs[s].copy_(matched_decode(new_q[s], k, v, table, lens, resources=res))
+
+    k0, v0, lens0 = k.clone(), v.clone(), lens.clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        loop()  # warm-up (also appends); restore the state before capture
+    torch.cuda.current_stream().wait_stream(side)
+    k.copy_(k0), v.copy_(v0), lens.copy_(lens0)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loop()
+    k.copy_(k0), v.copy_(v0), lens.copy_(lens0)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert lens.tolist() == [start + steps] * b
+    kh, vh, th = k.float().cpu().numpy(), v.float().cpu().numpy(), table.cpu().numpy()
+    for s in (0, steps // 2, steps - 1):
+        n = np.full(b, start + s + 1, dtype=np.int32)
+        expected = oracle.dense_reference(new_q[s].float().cpu().numpy(), kh, vh, th, n)
+        assert_out_close(outs[s], expected, f"step {s}")
+    del graph
