@@ -13,9 +13,9 @@ the single-GPU config the metric is quoted on.
   CUDA events, max over ranks.  When a config's KV pool is smaller than 2x L2,
   steps rotate over independent input copies so every step reads HBM.
 * ``e2e``: the same metric through the public API (``matched_decode``) with
-  host buffers: each step copies q / block table / lengths from pinned host
-  memory, decodes and copies the output back.  The KV cache is resident
-  device state, as in serving.
+  host buffers: each step copies q / block table / lengths from one pinned
+  host staging buffer (one H2D copy), decodes and copies the output back.
+  The KV cache is resident device state, as in serving.
 * ``roofline``: the partition kernel alone (K launches per graph window) vs
   the measured HBM copy bandwidth in MEASURED_PEAKS.json; ``traffic`` is the
   per-launch DRAM bytes of the ncu summary committed under profiles/.
@@ -127,11 +127,16 @@ def sweep(reps=20):
                 torch.cuda.empty_cache()
 
 
-def config_splits(name, args):
-    """Split count of the matched plan per config (0 = the plan's own heuristic)."""
+def config_plan(name, args, spec, sm_count):
+    """Split plan per config: cfg2 keeps its specified 1024-token partitions, --splits
+    asks the reference heuristic for an explicit count, otherwise this library's
+    B200 plan (``make_b200_plan``)."""
+    from paged_decode.splitkv_plan import make_b200_plan, make_splitkv_plan
     if args.splits is not None:
-        return args.splits
-    return {"cfg1": 0, "cfg2": 2, "cfg3": 0, "cfg4": 0, "cfg5": 16}[name]
+        return make_splitkv_plan(spec, sm_count, num_splits=args.splits)
+    if name == "cfg2":
+        return make_splitkv_plan(spec, sm_count, num_splits=2)
+    return make_b200_plan(spec, sm_count)
 
 
 # ---------------------------------------------------------------- CPU legs
@@ -317,7 +322,7 @@ def main():
         first.k, first.v, first.table = k_loc, v_loc, t_loc
         torch.cuda.empty_cache()
         cp = parallel.ContextParallelDecode(first.spec, device, kernel=args.kernel,
-                                            local_splits=config_splits(args.config, args))
+                                            local_splits=args.splits or 0)
         copies, wls = 1, [first]
         cp(first.q, k_loc, v_loc, t_loc, first.lengths)
         plan = cp.plan
@@ -336,8 +341,9 @@ def main():
         wls = [first] + [make_workload(args.config, device=device, batch=args.batch,
                                        context=args.context, rank=rank, seed=c)
                          for c in range(1, copies)]
-        res = allocate_matched_resources(first.spec, device,
-                                         num_splits=config_splits(args.config, args))
+        res = allocate_matched_resources(
+            first.spec, device,
+            plan=config_plan(args.config, args, first.spec, ops.sm_count(device)))
         plan = res.plan
         local_bytes = kv_bytes
 
@@ -348,7 +354,8 @@ def main():
         part_args = [ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
                                      tokens_per_split=plan.tokens_per_split, splits=plan.splits,
                                      protocol=ops.PROTOCOL_LSE, kernel=args.kernel, out=res.out,
-                                     partial=res.partials, lse=res.lse) for w in wls]
+                                     partial=res.partials, lse=res.lse, counters=res.counters,
+                                     flags=ops.FLAG_DYNAMIC) for w in wls]
         out_buf = res.out
 
     def step(i):
@@ -413,22 +420,35 @@ def main():
         else "simt"
     traffic, traffic_src = committed_traffic(args.config, kernel_name)
 
-    # e2e: public API with host buffers (pinned), copies inside the timed region.
-    hosts = []
-    for w in wls:
-        hq = torch.empty(w.q.shape, dtype=w.q.dtype).pin_memory()
-        hq.copy_(w.q)
-        hosts.append((hq, w.table.cpu().pin_memory(), w.lengths.cpu().pin_memory()))
+    # e2e: public API with host buffers.  Each step's inputs (q, block table,
+    # lengths) sit in one pinned staging buffer, copied to the device with one
+    # H2D copy (the workload tensors are views into its device twin, as a
+    # serving engine stages them); the output is copied back to pinned memory.
+    def staged(w):
+        parts = [w.q, w.table, w.lengths]
+        sizes = [t.numel() * t.element_size() for t in parts]
+        offs, total = [], 0
+        for n in sizes:
+            offs.append(total)
+            total += -(-n // 16) * 16
+        dev = torch.empty(total, dtype=torch.uint8, device=device)
+        views = [dev[o:o + n].view(t.dtype).view(t.shape) for o, n, t in zip(offs, sizes, parts)]
+        for v, t in zip(views, parts):
+            v.copy_(t)
+        w.q, w.table, w.lengths = views
+        host = torch.empty(total, dtype=torch.uint8).pin_memory()
+        host.copy_(dev)
+        return dev, host
+
+    stages = [staged(w) for w in wls]
     hout = torch.empty(out_buf.shape, dtype=out_buf.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in hosts[0])
+    h2d = stages[0][0].numel()
     d2h = hout.numel() * hout.element_size()
 
     def e2e_step(i):
-        w, (hq, ht, hl) = wls[i % copies], hosts[i % copies]
-        w.q.copy_(hq, non_blocking=True)
-        w.table.copy_(ht, non_blocking=True)
-        w.lengths.copy_(hl, non_blocking=True)
-        hout.copy_(decode_call(w), non_blocking=True)
+        dev, host = stages[i % copies]
+        dev.copy_(host, non_blocking=True)
+        hout.copy_(decode_call(wls[i % copies]), non_blocking=True)
 
     for i in range(3):
         e2e_step(i)

@@ -83,7 +83,14 @@ typedef enum PdlFlags {
    * programmatic dependent launch).  Needs `counters`, zero-initialised once; the
    * kernel leaves it zeroed.  The workspace is still written and the output
    * is bit-identical to the two-kernel path. */
-  PDL_FLAG_FUSED_MERGE = 4
+  PDL_FLAG_FUSED_MERGE = 4,
+  /* Work items are handed to the persistent CTAs from an atomic counter,
+   * partition-major (every row's first partition, then every second one...),
+   * instead of a static stride: balances batches of very different lengths.
+   * Uses counters[batch*num_heads] and [batch*num_heads + 1] (so `counters`
+   * needs batch*num_heads + 2 entries, zero-initialised once; the kernel
+   * leaves them zeroed).  Outputs are bit-identical to static scheduling. */
+  PDL_FLAG_DYNAMIC = 8
 } PdlFlags;
 
 /* Geometry contract; mirrors DecodeSpec (reference src/paged_decode/spec.py:11-30). */
@@ -135,7 +142,7 @@ typedef struct PdlDecodeArgs {
   float *maxima;              /* MLA protocol: [batch, num_heads, splits]          */
   float *denoms;              /*               [batch, num_heads, splits]          */
   float *accums;              /*               [batch, num_heads, splits, head_dim] */
-  int32_t *counters;          /* PDL_FLAG_FUSED_MERGE: int32 [batch * num_heads], zeroed */
+  int32_t *counters;          /* PDL_FLAG_FUSED_MERGE / _DYNAMIC: int32 [batch*num_heads + 2], zeroed */
 } PdlDecodeArgs;
 
 /* Partition kernel: per (row, KV head, partition) online softmax over the
@@ -247,6 +254,13 @@ int pdl_append_kv(const PdlAppendArgs *args, pdl_stream_t stream);
  * Replaces make_splitkv_plan (reference src/paged_decode/splitkv_plan.py:26-56). */
 int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,
                      PdlPlan *plan);
+
+/* Split plan for this library's persistent, dynamically scheduled kernels on
+ * `sm_count` SMs: about one work item per CTA slot, items of at most 4096
+ * tokens, partitions a multiple of the reference plan's tile.  No counterpart
+ * in the reference (its plan, pdl_splitkv_plan, is tuned for one CTA per
+ * partition on A100). */
+int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *plan);
 
 /* partitions = ceil(max_context_len/1024), table_width = ceil(max_context_len/256),
  * split workspace bytes = max_batch*num_heads*partitions*(head_dim+2)*4.

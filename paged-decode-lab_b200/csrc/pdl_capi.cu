@@ -285,6 +285,12 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream, bool fu
                     group_bytes <= 32 * 1024;
   p.counters = fuse ? a->counters : nullptr;
   if (did_fuse) *did_fuse = fuse;
+  // Dynamic scheduling (two words after the group counters of this batch)
+  // only pays when CTAs take more than one item each; a single-item launch
+  // would just add an atomic round trip before its first load.
+  p.sched = (a->flags & PDL_FLAG_DYNAMIC) && a->counters && items > 2LL * dev->sm_count
+                ? a->counters + (int64_t)a->batch * a->num_heads
+                : nullptr;
   const cudaError_t e = which == PDL_KERNEL_SIMT ? launch_partition_simt(L, stream)
                                                  : launch_partition_mma(L, stream);
   return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
@@ -417,6 +423,38 @@ extern "C" int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t n
   return PDL_OK;
 }
 
+// Split plan for this library's persistent, dynamically scheduled kernels:
+// about one work item per CTA slot (two CTAs per SM; measured best for
+// uniform batches), items of at most 4096 tokens so variable-length batches
+// balance, and never smaller than one tile (the partition sizes stay
+// multiples of the reference plan's tile, so the merge and workspace layouts
+// are unchanged).
+extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *plan) {
+  if (!spec || !plan) return PDL_ERR_NULL;
+  int st = pdl_spec_geometry(spec, nullptr, nullptr, nullptr);
+  if (st != PDL_OK) return st;
+  if (sm_count < 1) return PDL_ERR_SHAPE;
+  const int tile = spec->head_dim == 64 ? 256 : (spec->head_dim == 128 ? 128 : 64);
+  const int64_t capacity = ((int64_t)spec->max_context_len + 255) / 256 * 256;
+  const int64_t blocks = (capacity + tile - 1) / tile;
+  const int64_t groups = (int64_t)spec->max_batch * spec->num_kv_heads;
+  const int64_t slots = 2LL * sm_count;
+  int64_t splits = std::max<int64_t>((slots + groups / 2) / groups, (capacity + 4095) / 4096);
+  splits = std::min<int64_t>(std::max<int64_t>(splits, 1), blocks);
+  const int64_t tps = (blocks + splits - 1) / splits * tile;
+  splits = (capacity + tps - 1) / tps;  // drop partitions that would always be empty
+  int64_t padded = 1;
+  while (padded < splits) padded <<= 1;
+  plan->splits = (int32_t)splits;
+  plan->tile_tokens = tile;
+  plan->tokens_per_split = (int32_t)tps;
+  plan->table_capacity_tokens = (int32_t)capacity;
+  plan->lse_lanes = (int32_t)std::min<int64_t>(padded, 32);
+  plan->sm_count = sm_count;
+  plan->explicit_splits = 1;
+  return PDL_OK;
+}
+
 extern "C" int pdl_partition(const PdlDecodeArgs *args, pdl_stream_t stream) {
   int st = validate_common(args);
   if (st == PDL_OK) st = validate_partition_inputs(args);
@@ -476,6 +514,8 @@ extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) 
   if (st == PDL_OK) st = validate_out(args);
   if (st != PDL_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((args->flags & PDL_FLAG_DYNAMIC) && !args->counters)
+    return fail(PDL_ERR_WORKSPACE, "pdl_paged_decode", "dynamic scheduling needs counters");
   const bool direct = args->tokens_per_split == 0 ||
                       (args->splits == 1 && (args->flags & PDL_FLAG_DIRECT_SINGLE));
   if (direct) return run_partition(args, MODE_DIRECT, s);

@@ -47,6 +47,7 @@ struct PartitionParams {
   float *accums;
   uint32_t *fault;          // per-device fault word
   int32_t *counters;        // fused merge: finished items per (row, KV head, sub-group), or null
+  int32_t *sched;           // dynamic scheduling: [next item, finished CTAs], or null (static)
 };
 
 // Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],

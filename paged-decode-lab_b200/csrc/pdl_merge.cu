@@ -77,19 +77,30 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   const int lane = threadIdx.x & 31;
   const int unit = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
   const int row = unit / SLICES, col0 = (unit % SLICES) * CW;
-  grid_dependency_wait();
-  if (row >= p.rows) return;
+  // Lengths are an input of the decode, not an output of the partition
+  // kernel, so they are read before waiting for it.
   int live = p.splits;
-  if (p.lengths != nullptr) {
+  if (p.lengths != nullptr && row < p.rows) {
     const int len = __ldg(p.lengths + row / p.num_heads);
     live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
   }
+  grid_dependency_wait();
+  if (row >= p.rows) return;
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
   const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;
 
+  // Weights of partitions lane, lane+32, ... stay in registers (up to 128
+  // partitions; more are re-read).
+  constexpr int WR = 4;
+  float wreg[WR];
+#pragma unroll
+  for (int i = 0; i < WR; ++i)
+    wreg[i] = lane + 32 * i < live ? __ldcg(w_src + (lane + 32 * i) * p.w_part_stride) : -INFINITY;
   float mx = -INFINITY;
-  for (int s = lane; s < live; s += 32) mx = fmaxf(mx, __ldg(w_src + s * p.w_part_stride));
+#pragma unroll
+  for (int i = 0; i < WR; ++i) mx = fmaxf(mx, wreg[i]);
+  for (int s = lane + 32 * WR; s < live; s += 32) mx = fmaxf(mx, __ldcg(w_src + s * p.w_part_stride));
   mx = warp_max(mx);
   if (mx == -INFINITY) mx = 0.f;
 
@@ -97,13 +108,15 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   float scale = 1.f;  // final multiplier
   float tot = 0.f;
   if (lse_protocol) {
-    for (int s = lane; s < live; s += 32) tot += expf(__ldg(w_src + s * p.w_part_stride) - mx);
+#pragma unroll
+    for (int i = 0; i < WR; ++i) tot += lane + 32 * i < live ? expf(wreg[i] - mx) : 0.f;
+    for (int s = lane + 32 * WR; s < live; s += 32) tot += expf(__ldcg(w_src + s * p.w_part_stride) - mx);
     tot = warp_sum(tot);
     shift = tot > 0.f ? logf(tot) + mx : INFINITY;
   } else {
     const float *l_src = p.denoms + (int64_t)row * p.w_row_stride;
     for (int s = lane; s < live; s += 32)
-      tot += __ldg(l_src + s * p.w_part_stride) * expf(__ldg(w_src + s * p.w_part_stride) - mx);
+      tot += __ldcg(l_src + s * p.w_part_stride) * expf(__ldcg(w_src + s * p.w_part_stride) - mx);
     tot = warp_sum(tot);
     scale = 1.f / (tot > 0.f ? tot : 1.f);
   }
@@ -112,18 +125,24 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
   for (int s0 = 0; s0 < live; s0 += 32) {
-    const float wl = (s0 + lane < live) ? expf(__ldg(w_src + (s0 + lane) * p.w_part_stride) - shift)
-                                        : 0.f;
+    const int wi = s0 / 32;
+    // Register select (a dynamic index would put wreg in local memory).
+    const float wsrc = wi == 0 ? wreg[0] : wi == 1 ? wreg[1] : wi == 2 ? wreg[2]
+                     : wi == 3 ? wreg[3]
+                     : (s0 + lane < live ? __ldcg(w_src + (s0 + lane) * p.w_part_stride)
+                                         : -INFINITY);
+    const float wl = (s0 + lane < live) ? expf(wsrc - shift) : 0.f;
     const int n = min(32, live - s0);
-    // Rows of up to 8 partitions are loaded before any is consumed, so the
-    // memory round trips overlap instead of serialising per partition.
-    for (int k0 = 0; k0 < n; k0 += 8) {
-      float v[8][E];
+    // Rows of up to BATCH partitions are loaded before any is consumed, so
+    // the memory round trips overlap instead of serialising per partition.
+    constexpr int BATCH = E <= 4 ? 16 : 8;
+    for (int k0 = 0; k0 < n; k0 += BATCH) {
+      float v[BATCH][E];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < BATCH; ++j)
         load_cols<E>(r_src + (int64_t)(s0 + min(k0 + j, n - 1)) * p.part_stride + lane * E, v[j]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < BATCH; ++j) {
         const float wk = __shfl_sync(FULL_MASK, wl, min(k0 + j, 31));
         if (k0 + j < n) {
 #pragma unroll

@@ -108,8 +108,13 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   float *comb_ml = comb_acc + L::ACC_FLOATS;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFFSET);
   uint64_t *empty = full + NS;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + NS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET);
   volatile int *merge_flag = abort_flag + 1;
+  ItemRing ring;
+  ring.full = reinterpret_cast<uint64_t *>(smem + L::RING_OFFSET);
+  ring.empty = ring.full + IR;
+  ring.slot = reinterpret_cast<volatile int *>(ring.empty + IR);
+  ring.shared = abort_flag + 2;
   if (!smem_base_aligned(smem, p.fault)) return;
 
   // The merge kernel that follows may be scheduled now; it waits for this
@@ -121,13 +126,14 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
+    ring_init(ring);
     *abort_flag = 0;
     mbar_init_fence();
   }
   __syncthreads();
 
   if (warp == 0) {
-    run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, lane);
+    run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, ring, lane);
     return;
   }
 
@@ -143,18 +149,15 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   const bool q_vec = p.q_vec16 != 0;
   uint32_t it = 0;
 
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+  uint32_t ik = 0;
+  int static_next = blockIdx.x;
+  while (true) {
+    const int item = consumer_next<NC>(p, ring, ik, static_next, cw, lane, abort_flag);
+    if (item < 0) break;
     const Item w = decode_item(p, item);
     const int h0 = w.kvh * p.group + w.sub * GC;
     const int rows = min(GC, p.group - w.sub * GC);
-    const Range rg = item_range(p, w);
-    if (rg.start >= rg.stop) {
-      if (p.write_empty || p.mode == MODE_DIRECT)
-        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
-      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
-      continue;
-    }
-
+    // q is loaded before the row length is known, so both round trips overlap.
     // q of head (nt*8 + grp) as B fragments: dims kk*16 + quad*2 + {0,1} and +8.
     uint32_t qf[NT][KS][2];
 #pragma unroll
@@ -168,6 +171,14 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
         qf[nt][kk][0] = valid ? load_q_pair(qrow + kk * 16 + quad * 2, q_vec) : 0u;
         qf[nt][kk][1] = valid ? load_q_pair(qrow + kk * 16 + quad * 2 + 8, q_vec) : 0u;
       }
+    }
+
+    const Range rg = item_range(p, w);
+    if (rg.start >= rg.stop) {
+      if (p.write_empty || p.mode == MODE_DIRECT)
+        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
+      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
+      continue;
     }
 
     // Running state for heads nt*8 + quad*2 + {0,1}; acc[nt][dm] holds

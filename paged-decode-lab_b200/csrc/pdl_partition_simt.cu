@@ -55,8 +55,13 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   float *comb_ml = comb_acc + L::ACC_FLOATS;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFFSET);
   uint64_t *empty = full + NS;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + NS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET);
   volatile int *merge_flag = abort_flag + 1;
+  ItemRing ring;
+  ring.full = reinterpret_cast<uint64_t *>(smem + L::RING_OFFSET);
+  ring.empty = ring.full + IR;
+  ring.slot = reinterpret_cast<volatile int *>(ring.empty + IR);
+  ring.shared = abort_flag + 2;
   static_assert(L::BYTES <= kTwoCtaSmemBytes, "two CTAs per SM");
   if (!smem_base_aligned(smem, p.fault)) return;
 
@@ -69,13 +74,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
+    ring_init(ring);
     *abort_flag = 0;
     mbar_init_fence();
   }
   __syncthreads();
 
   if (warp == 0) {
-    run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, lane);
+    run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, ring, lane);
     return;
   }
 
@@ -89,18 +95,15 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const int tid = cw * 32 + lane;
   uint32_t it = 0;
 
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+  uint32_t ik = 0;
+  int static_next = blockIdx.x;
+  while (true) {
+    const int item = consumer_next<NC>(p, ring, ik, static_next, cw, lane, abort_flag);
+    if (item < 0) break;
     const Item w = decode_item(p, item);
     const int h0 = w.kvh * p.group + w.sub * GC;
     const int rows = min(GC, p.group - w.sub * GC);
-    const Range rg = item_range(p, w);
-    if (rg.start >= rg.stop) {
-      if (p.write_empty || p.mode == MODE_DIRECT)
-        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
-      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
-      continue;
-    }
-
+    // q is loaded before the row length is known, so both round trips overlap.
     // q chunk j of every head of the sub-group, as FP32 pairs.
     float2 q2[GC][4];
 #pragma unroll
@@ -121,6 +124,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) q2[g][e] = bf16x2_to_float2(raw[e]);
+    }
+
+    const Range rg = item_range(p, w);
+    if (rg.start >= rg.stop) {
+      if (p.write_empty || p.mode == MODE_DIRECT)
+        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
+      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
+      continue;
     }
 
     float m[GC], l[GC];

@@ -11,12 +11,23 @@ struct Item {
   int b, kvh, sub, split;
 };
 
-// item = ((b * num_kv_heads + kvh) * nsub + sub) * splits + split
+// Static order:  item = ((b * num_kv_heads + kvh) * nsub + sub) * splits + split
+// (a CTA's consecutive items are neighbouring partitions of one row).
+// Dynamic order: item = split * (batch * num_kv_heads * nsub) + group, so every
+// row's first partition is handed out before any row's second one and the
+// last items are the tail partitions of the longest rows.
 __device__ __forceinline__ Item decode_item(const PartitionParams &p, int item) {
   Item it;
-  it.split = item % p.splits;
-  const int rest = item / p.splits;
   const int per_row = p.num_kv_heads * p.nsub;
+  int rest;
+  if (p.sched != nullptr) {
+    const int groups = p.batch * per_row;
+    it.split = item / groups;
+    rest = item % groups;
+  } else {
+    it.split = item % p.splits;
+    rest = item / p.splits;
+  }
   it.b = rest / per_row;
   const int r = rest % per_row;
   it.kvh = r / p.nsub;
@@ -65,15 +76,99 @@ __device__ void store_empty(const PartitionParams &p, int b, int h0, int rows, i
   }
 }
 
+// ------------------------------------------------------------- work items
+// Static scheduling: CTA c takes items c, c + gridDim.x, ...  Dynamic
+// scheduling (p.sched != null): the producer warp takes the next item from a
+// global atomic counter and publishes it in an IR-deep shared-memory ring;
+// one consumer thread (the leader) takes it from the ring and hands it to all
+// consumer warps through a named barrier, so every warp processes the same
+// sequence even if a bounded wait gives up (the leader then hands out "stop").
+constexpr int IR = 8;
+
+struct ItemRing {
+  uint64_t *full;       // [IR] producer -> consumers, count 1
+  uint64_t *empty;      // [IR] consumers -> producer, count 1 (the leader)
+  volatile int *slot;   // [IR] item indices (-1 = no more items)
+  volatile int *shared; // item handed to the consumer warps
+};
+
+__device__ __forceinline__ void ring_init(const ItemRing &r) {
+  for (int i = 0; i < IR; ++i) {
+    mbar_init(&r.full[i], 1);
+    mbar_init(&r.empty[i], 1);
+  }
+}
+
+// Next item of the producer warp (all lanes return it); -1 when done.
+__device__ __forceinline__ int producer_next(const PartitionParams &p, const ItemRing &r,
+                                             uint32_t &k, int &static_next, int lane,
+                                             volatile int *abort_flag) {
+  if (p.sched == nullptr) {
+    const int item = static_next;
+    static_next += gridDim.x;
+    return item < p.n_items ? item : -1;
+  }
+  int item = -1;
+  if (lane == 0) {
+    item = atomicAdd(p.sched, 1);
+    if (item >= p.n_items) item = -1;
+    const int s = k % IR;
+    if (k >= IR)
+      pipeline_wait(&r.empty[s], ((k / IR) & 1) ^ 1, p.fault, FAULT_PRODUCER_EMPTY_WAIT, abort_flag);
+    r.slot[s] = item;
+    mbar_arrive(&r.full[s]);
+  }
+  ++k;
+  return __shfl_sync(FULL_MASK, item, 0);
+}
+
+// The producer's exit: count this CTA as finished; the last one resets the
+// scheduler words for the next launch (every CTA's final fetch precedes its
+// count, and no fetch follows the last count).
+__device__ __forceinline__ void producer_finish(const PartitionParams &p, int lane) {
+  if (p.sched == nullptr || lane != 0) return;
+  __threadfence();
+  if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+    atomicExch(p.sched, 0);
+    atomicExch(p.sched + 1, 0);
+  }
+}
+
+// Next item of the consumer warps (identical in every consumer warp); -1 when done.
+template <int NC>
+__device__ __forceinline__ int consumer_next(const PartitionParams &p, const ItemRing &r,
+                                             uint32_t &k, int &static_next, int cw, int lane,
+                                             volatile int *abort_flag) {
+  if (p.sched == nullptr) {
+    const int item = static_next;
+    static_next += gridDim.x;
+    return item < p.n_items ? item : -1;
+  }
+  if (cw == 0 && lane == 0) {
+    const int s = k % IR;
+    int item = -1;
+    if (pipeline_wait(&r.full[s], (k / IR) & 1, p.fault, FAULT_CONSUMER_FULL_WAIT, abort_flag))
+      item = r.slot[s];
+    *r.shared = (item >= 0 && item < p.n_items) ? item : -1;
+    mbar_arrive(&r.empty[s]);
+  }
+  ++k;
+  named_barrier(1, NC * 32);
+  const int item = *r.shared;
+  named_barrier(1, NC * 32);  // all warps read it before the leader writes the next one
+  return item;
+}
+
 // Producer warp: for every item of this CTA, in the consumers' order, read
-// the live block-table entries (32 per load, one per lane, never past
-// ceil(stop/256)) and issue one T-token tile of K and V per stage as
-// D/64 TMA boxes each.  T divides 256, so a tile never spans two pages.
+// the partition's block-table entries (32 per load, one per lane, never past
+// the table width; only entries of live pages are used) and issue one
+// T-token tile of K and V per stage as D/64 TMA boxes each.  T divides 256,
+// so a tile never spans two pages.
 template <int D, int T, int NS>
 __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
                              const PartitionParams &p, uint8_t *kbuf, uint8_t *vbuf,
                              uint64_t *full, uint64_t *empty, volatile int *abort_flag,
-                             int lane) {
+                             const ItemRing &ring, int lane) {
   constexpr int SUBTILES = D / 64;
   constexpr int SUB_BYTES = T * 128;
   constexpr int TILE_BYTES = T * D * 2;
@@ -82,23 +177,30 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
     prefetch_tensormap(k_map);
     prefetch_tensormap(v_map);
   }
-  uint32_t it = 0;
+  uint32_t it = 0, k = 0;
+  int static_next = blockIdx.x;
   bool ok = true;
-  for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+  while (ok) {
+    const int item = producer_next(p, ring, k, static_next, lane, abort_flag);
+    if (item < 0) break;
     const Item w = decode_item(p, item);
+    // The first 32 table entries of the partition are read together with the
+    // row length (speculatively, but never past the table's width), so the
+    // two round trips overlap; entries past the live pages are never used.
+    const int32_t *trow = p.table + (int64_t)w.b * p.table_stride;
+    const int64_t first_tok = (int64_t)w.split * p.tokens_per_split;
+    int base = first_tok < (int64_t)p.table_width * 256 ? (int)(first_tok >> 8) : -64;
+    int my_page = (base >= 0 && base + lane < p.table_width) ? __ldg(trow + base + lane) : 0;
     const Range r = item_range(p, w);
     if (r.start >= r.stop) continue;
     const int t0 = r.start / T * T;
     const int ntiles = (r.stop - t0 + T - 1) / T;
-    const int live_pages = (r.stop + 255) >> 8;
-    const int32_t *trow = p.table + (int64_t)w.b * p.table_stride;
-    int base = -64, my_page = 0;
     for (int i = 0; i < ntiles; ++i, ++it) {
       const int tok = t0 + i * T;
       const int pg = tok >> 8;
-      if (pg >= base + 32) {
+      if (base < 0 || pg >= base + 32) {
         base = pg;
-        my_page = (pg + lane < live_pages) ? __ldg(trow + pg + lane) : 0;
+        my_page = (pg + lane < p.table_width) ? __ldg(trow + pg + lane) : 0;
       }
       const int page = __shfl_sync(FULL_MASK, my_page, pg - base);
       if (lane == 0) {
@@ -122,11 +224,24 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
     }
   }
   if (!ok && lane == 0) {
-    // Let the copies already issued land before the CTA exits.
+    // Let the copies already issued land before the CTA exits, and tell the
+    // consumers there is nothing more.
     const uint32_t first = it > NS ? it - NS : 0;
-    for (uint32_t k = first; k < it; ++k)
-      mbar_wait_bounded(&full[k % NS], (k / NS) & 1, p.fault, FAULT_DRAIN_WAIT);
+    for (uint32_t j = first; j < it; ++j)
+      mbar_wait_bounded(&full[j % NS], (j / NS) & 1, p.fault, FAULT_DRAIN_WAIT);
   }
+  if (!ok && p.sched != nullptr && lane == 0) {
+    while (true) {  // publish "stop" so the consumer leader need not time out
+      const int s = k % IR;
+      if (k >= IR && !mbar_wait_bounded(&ring.empty[s], ((k / IR) & 1) ^ 1, p.fault,
+                                        FAULT_PRODUCER_EMPTY_WAIT))
+        break;
+      ring.slot[s] = -1;
+      mbar_arrive(&ring.full[s]);
+      break;
+    }
+  }
+  producer_finish(p, lane);
 }
 
 // Merge NC per-warp softmax states of one item and store the outputs.
@@ -296,6 +411,8 @@ __device__ __forceinline__ bool smem_base_aligned(const void *smem, uint32_t *fa
 
 // Shared-memory plan of a partition kernel: K ring | V ring | per-warp
 // accumulators [NC][GC][D] | per-warp (m, l) [NC][2][GC] | mbarriers | flag.
+// Tail after the mbarriers: item ring barriers [2][IR], item slots [IR],
+// then abort flag, merge flag and the handed-out item (16 bytes).
 template <int D, int T, int NS, int NC, int GC>
 struct PartitionSmem {
   static constexpr int TILE_BYTES = T * D * 2;
@@ -303,7 +420,9 @@ struct PartitionSmem {
   static constexpr int ACC_FLOATS = NC * GC * D;
   static constexpr int ML_FLOATS = NC * 2 * GC;
   static constexpr int BAR_OFFSET = KV_BYTES + (ACC_FLOATS + ML_FLOATS) * 4;
-  static constexpr int BYTES = BAR_OFFSET + 2 * NS * 8 + 16;
+  static constexpr int RING_OFFSET = BAR_OFFSET + 2 * NS * 8;
+  static constexpr int FLAG_OFFSET = RING_OFFSET + 2 * IR * 8 + IR * 4;
+  static constexpr int BYTES = FLAG_OFFSET + 16;
   static_assert(TILE_BYTES % 1024 == 0, "swizzled tiles need 1024-byte alignment");
   static_assert((T * 128) % 1024 == 0, "swizzled sub-tiles need 1024-byte alignment");
   static_assert((GC * D * 4) % 16 == 0, "per-warp accumulators are accessed as float4");

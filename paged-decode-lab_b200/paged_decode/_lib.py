@@ -18,11 +18,12 @@ STATUS_NAMES = {
 }
 PROTOCOL_LSE, PROTOCOL_MLA = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
-FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE = 1, 2, 4
+FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE, FLAG_DYNAMIC = 1, 2, 4, 8
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
 SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode", "pdl_append_kv",
-           "pdl_paged_decode_static_scratch", "pdl_splitkv_plan", "pdl_spec_geometry",
+           "pdl_paged_decode_static_scratch", "pdl_splitkv_plan", "pdl_b200_plan",
+           "pdl_spec_geometry",
            "pdl_status_string", "pdl_last_error", "pdl_abi_version", "pdl_read_fault")
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -94,6 +95,8 @@ def load():
     lib.pdl_lse_merge.restype = ctypes.c_int
     lib.pdl_splitkv_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, _i32, ctypes.POINTER(PdlPlan)]
     lib.pdl_splitkv_plan.restype = ctypes.c_int
+    lib.pdl_b200_plan.argtypes = [ctypes.POINTER(PdlSpec), _i32, ctypes.POINTER(PdlPlan)]
+    lib.pdl_b200_plan.restype = ctypes.c_int
     lib.pdl_spec_geometry.argtypes = [ctypes.POINTER(PdlSpec), ctypes.POINTER(_i32),
                                       ctypes.POINTER(_i32), ctypes.POINTER(_i64)]
     lib.pdl_spec_geometry.restype = ctypes.c_int

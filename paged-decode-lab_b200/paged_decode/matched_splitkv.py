@@ -24,17 +24,26 @@ class MatchedResources:
     out: torch.Tensor
     partials: torch.Tensor
     lse: torch.Tensor
-    # Group counters of the fused partition+merge kernel (zeroed; the kernel
-    # leaves them zeroed).  None selects the two-kernel launch.
+    # Group counters of the fused partition+merge kernel plus the two words of
+    # the dynamic scheduler (zeroed; the kernels leave them zeroed).  None
+    # selects the two-kernel launch with static scheduling.
     counters: torch.Tensor | None = None
 
 
-def allocate_matched_resources(spec, device, *, num_splits=0):
-    """out bf16 [B,Hq,D]; partials f32 [B,Hq,S,D]; lse f32 [B,Hq,S] (matched_splitkv.py:24-34)."""
+def allocate_matched_resources(spec, device, *, num_splits=0, plan=None):
+    """out bf16 [B,Hq,D]; partials f32 [B,Hq,S,D]; lse f32 [B,Hq,S] (matched_splitkv.py:24-34).
+
+    ``plan`` (optional, not in the reference) supplies a ready split plan, e.g.
+    ``make_b200_plan(spec, sm_count)``; otherwise the reference heuristic runs
+    for this device's SM count with ``num_splits``.
+    """
     device = torch.device(device)
     if device.type != "cuda":
         raise ValueError("matched resources require CUDA")
-    plan = make_splitkv_plan(spec, ops.sm_count(device), num_splits=num_splits)
+    if plan is None:
+        plan = make_splitkv_plan(spec, ops.sm_count(device), num_splits=num_splits)
+    elif plan.splits * plan.tokens_per_split < spec.table_width * 256:
+        raise ValueError("plan does not cover the table capacity")
     shape = (spec.max_batch, spec.num_heads, plan.splits)
     return MatchedResources(
         spec, plan,
@@ -42,7 +51,7 @@ def allocate_matched_resources(spec, device, *, num_splits=0):
                     dtype=torch.bfloat16),
         torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32),
         torch.empty(shape, device=device, dtype=torch.float32),
-        torch.zeros(spec.max_batch * spec.num_heads, device=device, dtype=torch.int32))
+        torch.zeros(spec.max_batch * spec.num_heads + 2, device=device, dtype=torch.int32))
 
 
 def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="auto"):
@@ -77,7 +86,8 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
                            protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
                            partial=resources.partials, lse=resources.lse,
                            counters=resources.counters,
-                           flags=0 if resources.counters is None else ops.FLAG_FUSED_MERGE)
+                           flags=0 if resources.counters is None
+                           else ops.FLAG_FUSED_MERGE | ops.FLAG_DYNAMIC)
     ops.paged_decode(args, q.device)
     cache.put(key, args)
     return resources.out

@@ -117,8 +117,9 @@ class ContextParallelDecode:
     """
 
     def __init__(self, spec, device, group=None, local_splits=0, kernel="auto"):
+        """``local_splits`` 0 uses the B200 plan for the rank-local capacity."""
         from . import ops
-        from .splitkv_plan import make_splitkv_plan
+        from .splitkv_plan import make_b200_plan, make_splitkv_plan
         self.ops = ops
         self.group = group
         self.world = dist.get_world_size(group)
@@ -129,8 +130,9 @@ class ContextParallelDecode:
         self.per_rank = tokens_per_rank(spec.table_width, self.world)
         self.local_spec = DecodeSpec(spec.max_batch, spec.num_heads, spec.num_kv_heads,
                                      spec.head_dim, self.per_rank)
-        self.plan = make_splitkv_plan(self.local_spec, ops.sm_count(self.device),
-                                      num_splits=local_splits)
+        sms = ops.sm_count(self.device)
+        self.plan = (make_b200_plan(self.local_spec, sms) if not local_splits else
+                     make_splitkv_plan(self.local_spec, sms, num_splits=local_splits))
         b, hq, d, s = spec.max_batch, spec.num_heads, spec.head_dim, self.plan.splits
         f32 = dict(device=self.device, dtype=torch.float32)
         self.partials = torch.empty(b, hq, s, d, **f32)
@@ -140,6 +142,8 @@ class ContextParallelDecode:
         self.gathered = torch.zeros(self.world * self.layout.block, **f32)
         self.out = torch.empty(b, hq, d, device=self.device, dtype=torch.bfloat16)
         self.local_len = torch.zeros(b, device=self.device, dtype=torch.int32)
+        # Dynamic-scheduler words of the local partition launch (left zeroed).
+        self.counters = torch.zeros(b * hq + 2, device=self.device, dtype=torch.int32)
         self._args = {}
 
     def _launch_args(self, q, k_local, v_local, table_local, scale):
@@ -151,7 +155,8 @@ class ContextParallelDecode:
             part = ops.decode_args(q, k_local, v_local, table_local, self.local_len, scale=scale,
                                    tokens_per_split=self.plan.tokens_per_split, splits=s,
                                    protocol=ops.PROTOCOL_LSE, kernel=self.kernel,
-                                   partial=self.partials, lse=self.lse)
+                                   partial=self.partials, lse=self.lse, counters=self.counters,
+                                   flags=ops.FLAG_DYNAMIC)
             send_p, send_l = self.layout.send_views(self.send)
             local = ops.merge_args(self.partials, self.lse, rows=rows, parts=s, head_dim=d,
                                    row_stride=s * d, part_stride=d, lse_row_stride=s,

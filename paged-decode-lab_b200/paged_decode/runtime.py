@@ -34,8 +34,8 @@ class Resources:
     maxima: torch.Tensor | None = None
     denoms: torch.Tensor | None = None
     accums: torch.Tensor | None = None
-    # Group counters of the fused partition+merge kernel (zeroed, split
-    # backends only; the kernel leaves them zeroed).
+    # Group counters of the fused partition+merge kernel plus the dynamic
+    # scheduler's two words (zeroed, split backends only; left zeroed).
     counters: torch.Tensor | None = None
 
 
@@ -55,7 +55,7 @@ def allocate_resources(spec, device, backend="triton_splitk"):
         result.maxima = torch.empty(shape, device=device, dtype=torch.float32)
         result.denoms = torch.empty(shape, device=device, dtype=torch.float32)
         result.accums = torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32)
-        result.counters = torch.zeros(spec.max_batch * spec.num_heads, device=device,
+        result.counters = torch.zeros(spec.max_batch * spec.num_heads + 2, device=device,
                                       dtype=torch.int32)
     return result
 
@@ -169,7 +169,8 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
                                protocol=ops.PROTOCOL_MLA, kernel=kernel, out=resources.out,
                                maxima=resources.maxima, denoms=resources.denoms,
                                accums=resources.accums, counters=resources.counters,
-                               flags=0 if resources.counters is None else ops.FLAG_FUSED_MERGE)
+                               flags=0 if resources.counters is None
+                               else ops.FLAG_FUSED_MERGE | ops.FLAG_DYNAMIC)
     else:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)

@@ -38,3 +38,22 @@ def make_splitkv_plan(spec, sm_count, *, num_splits=0):
     return SplitKVPlan(plan.splits, plan.tile_tokens, plan.tokens_per_split,
                        plan.table_capacity_tokens, plan.lse_lanes, plan.sm_count,
                        "explicit" if plan.explicit_splits else "pinned_geometry")
+
+
+def make_b200_plan(spec, sm_count):
+    """Split plan for this library's persistent kernels (``pdl_b200_plan``).
+
+    About one work item per CTA slot (two CTAs per SM), items of at most
+    4096 tokens so variable-length batches balance under dynamic scheduling,
+    partitions a multiple of the reference plan's tile.  Use it through
+    ``allocate_matched_resources(spec, device, num_splits=plan.splits)``.
+    """
+    if type(sm_count) is not int or sm_count < 1:
+        raise ValueError("positive SM count required")
+    plan = _lib.PdlPlan()
+    status = _lib.load().pdl_b200_plan(ctypes.byref(_lib.make_spec(spec)), sm_count,
+                                       ctypes.byref(plan))
+    if status != _lib.PDL_OK:
+        raise ValueError(f"invalid plan request: {_lib.status_text(status)}")
+    return SplitKVPlan(plan.splits, plan.tile_tokens, plan.tokens_per_split,
+                       plan.table_capacity_tokens, plan.lse_lanes, plan.sm_count, "b200")

@@ -154,3 +154,17 @@ def test_graph_nodes_are_counted_as_logical_operators():
 def test_invalid_denominators_cannot_produce_latency(args):
     with pytest.raises(ValueError):
         interval_per_operator(*args)
+
+
+def test_b200_plan_invariants():
+    from paged_decode.splitkv_plan import make_b200_plan
+    for b, hq, hkv, d, cap in [(4, 8, 2, 128, 1024), (64, 32, 32, 64, 2048), (1, 16, 4, 256, 2320),
+                               (32, 16, 4, 256, 2320), (128, 32, 8, 128, 32768),
+                               (2, 64, 8, 128, 524288), (1, 1, 1, 64, 1)]:
+        plan = make_b200_plan(DecodeSpec(b, hq, hkv, d, cap), 148)
+        capacity = -(-cap // 256) * 256
+        assert plan.tokens_per_split % plan.tile_tokens == 0
+        assert plan.splits * plan.tokens_per_split >= capacity
+        assert (plan.splits - 1) * plan.tokens_per_split < capacity  # no always-empty partition
+        assert plan.tokens_per_split <= max(4096, plan.tile_tokens)
+    assert make_b200_plan(DecodeSpec(128, 32, 8, 128, 32768), 148).splits == 8

@@ -166,7 +166,7 @@ def test_fused_merge_equals_two_kernel_path(kernel, protocol, skip_empty):
     """One kernel (last CTA of a group merges) == partition + merge kernels, bit for bit."""
     case = cases.make_case([3000, 0, 1, 4096, 257], 8, 2, 128, seed=12, capacity=4096)
     q, k, v, table, lens = device_case(case)
-    counters = torch.zeros(5 * 8, dtype=torch.int32, device="cuda")
+    counters = torch.zeros(5 * 8 + 2, dtype=torch.int32, device="cuda")
     outs = []
     for fused in (False, True):
         out = torch.empty(5, 8, 128, dtype=torch.bfloat16, device="cuda")
@@ -185,3 +185,31 @@ def test_fused_merge_equals_two_kernel_path(kernel, protocol, skip_empty):
     assert torch.equal(outs[0], outs[1])
     assert not counters.any()
     assert_out_close(outs[1], oracle.dense_reference(*case.arrays(), scale=0.09))
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_dynamic_scheduling_is_bit_identical_to_static(kernel):
+    """Atomic, partition-major item hand-out changes which CTA does what, not a bit."""
+    lengths = [0, 32768, 1, 4000, 9999, 257, 0, 20000]  # 512 items: > 2 per CTA slot
+    rows = len(lengths)
+    case = cases.make_case(lengths, 8, 2, 128, seed=13, capacity=32768, pool_factor=1.0)
+    q, k, v, table, lens = device_case(case)
+    counters = torch.zeros(rows * 8 + 2, dtype=torch.int32, device="cuda")
+    outs = []
+    for flags in (0, ops.FLAG_DYNAMIC, ops.FLAG_DYNAMIC | ops.FLAG_SKIP_EMPTY):
+        out = torch.empty(rows, 8, 128, dtype=torch.bfloat16, device="cuda")
+        partial = torch.empty(rows, 8, 32, 128, device="cuda")
+        lse = torch.empty(rows, 8, 32, device="cuda")
+        args = ops.decode_args(q, k, v, table, lens, scale=0.088, tokens_per_split=1024,
+                               splits=32, protocol=ops.PROTOCOL_LSE, kernel=kernel, flags=flags,
+                               out=out, partial=partial, lse=lse, counters=counters)
+        for _ in range(2):  # the scheduler words reset themselves between launches
+            ops.paged_decode(args, q.device)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert not counters.any()
+    few = [0, 1, 2, 3]
+    sub = oracle.dense_reference(case.q[few], case.k, case.v, case.table[few], case.lengths[few],
+                                 scale=0.088)
+    assert_out_close(outs[1][few], sub)
