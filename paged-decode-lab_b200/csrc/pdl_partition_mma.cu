@@ -204,12 +204,17 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       if (r0 < hi && r0 + TW > lo) {
         const uint32_t ks = kbase + s * S::TILE_BYTES;
         const uint32_t vs = vbase + s * S::TILE_BYTES;
-        // ---- S^T = K . Q^T
-        float sc[MT][NT][4];
+        // ---- S^T = K . Q^T, accumulated in CH independent chains (slices of D
+        // interleaved) so consecutive MMAs do not wait on each other.
+        constexpr int CH = KS >= 16 ? 4 : 2;
+        float part[CH][MT][NT][4];
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+        for (int c = 0; c < CH; ++c)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              part[c][mt][nt][0] = part[c][mt][nt][1] = part[c][mt][nt][2] = part[c][mt][nt][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const int chunk = kk * 2 + k_chunk;
@@ -218,9 +223,22 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
             uint32_t a[4];
             ldsm_x4(ks + (chunk >> 3) * S::SUB_BYTES + swizzle128(r0 + mt * 16 + k_row, chunk & 7), a);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma_bf16(sc[mt][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+            for (int nt = 0; nt < NT; ++nt)
+              mma_bf16(part[kk % CH][mt][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
           }
         }
+        float sc[MT][NT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float v = part[0][mt][nt][e];
+#pragma unroll
+              for (int c = 1; c < CH; ++c) v += part[c][mt][nt][e];
+              sc[mt][nt][e] = v;
+            }
         // ---- mask rows outside [lo, hi) and fold in the scale (base 2)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
