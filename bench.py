@@ -61,7 +61,10 @@ def parse_args():
     ap.add_argument("--kernel", default="auto", choices=("auto", "simt", "mma"))
     ap.add_argument("--mode", default="batch", choices=("batch", "context"),
                     help="N>1: independent batch per rank (weak) or one batch split by context "
-                         "across ranks with an NCCL all-gather (strong)")
+                         "across ranks (strong)")
+    ap.add_argument("--exchange", default="p2p", choices=("nccl", "p2p"),
+                    help="context mode: NCCL all-gather between two merge kernels, or one "
+                         "kernel storing into peers' buffers over NVLink (pdl_exchange_merge)")
     ap.add_argument("--hot", action="store_true",
                     help="reuse one input copy every step (L2-resident when it fits), as the "
                          "reference measured its A100 numbers; default rotates copies past L2")
@@ -71,6 +74,10 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true",
                     help="partition-kernel GB/s for every (head_dim, group, kernel) at ~1 GB of "
                          "KV (one JSON line per point; not the contract line)")
+    ap.add_argument("--exchange-micro", action="store_true",
+                    help="under torchrun (N>1): time the context-parallel combine alone, NCCL "
+                         "path (local merge, all-gather, merge) vs the peer-memory exchange "
+                         "kernel (one JSON line per shape; not the contract line)")
     return ap.parse_args()
 
 
@@ -265,6 +272,87 @@ def reference_line(args):
                     "d2h_bytes_per_step": 0}}
 
 
+def exchange_micro(reps=20, steps=20):
+    """Context-parallel combine alone on every rank, graph-timed, max over ranks:
+    rows = B*Hq merged over `splits` local partitions, then across the ranks."""
+    import torch
+    import torch.distributed as dist
+    from paged_decode import ops, parallel
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+
+    def timed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(steps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (reps * steps)], device=dev,
+                         dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del graph
+        return round(t.item(), 2)
+
+    # (rows, local splits, head_dim): config 5 at 64k / 524k tokens per row,
+    # a wide batch, and the config-3 geometry.
+    for rows, splits, d in [(128, 19, 128), (128, 64, 128), (1024, 8, 128), (32, 40, 256)]:
+        gen = torch.Generator(device=dev).manual_seed(rank + 1)
+        partial = torch.randn(rows, splits, d, device=dev, generator=gen)
+        lse = torch.randn(rows, splits, device=dev, generator=gen)
+        out = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
+        layout = parallel.ExchangeLayout(rows, d, world)
+        send = torch.zeros(layout.block, device=dev)
+        gathered = torch.zeros(world * layout.block, device=dev)
+        sp, sl = layout.send_views(send)
+        lm = ops.merge_args(partial, lse, rows=rows, parts=splits, head_dim=d,
+                            row_stride=splits * d, part_stride=d, lse_row_stride=splits,
+                            lse_part_stride=1, out_partial=sp, out_lse=sl)
+        rs, ps, lrs, lps = layout.merge_strides()
+        gm = ops.merge_args(gathered, gathered[layout.lse_offset:], rows=rows, parts=world,
+                            head_dim=d, row_stride=rs, part_stride=ps, lse_row_stride=lrs,
+                            lse_part_stride=lps, out=out)
+
+        def nccl_path():
+            ops.lse_merge(lm, dev)
+            dist.all_gather_into_tensor(gathered, send)
+            ops.lse_merge(gm, dev)
+
+        peers = parallel.PeerExchange(rows, d, dev)
+        ea = ops.exchange_args(partial, lse, rows=rows, parts=splits, head_dim=d, rank=rank,
+                               world=world, buffers=peers.ptrs, out=out)
+        line = {"rows": rows, "splits": splits, "head_dim": d, "world": world,
+                "local_merge_us": timed(lambda: ops.lse_merge(lm, dev)),
+                "all_gather_us": timed(lambda: dist.all_gather_into_tensor(gathered, send)),
+                "global_merge_us": timed(lambda: ops.lse_merge(gm, dev)),
+                "nccl_path_us": timed(nccl_path),
+                "p2p_exchange_us": timed(lambda: ops.exchange_merge(ea, dev))}
+        torch.cuda.synchronize(dev)
+        line["fault_word"] = ops.read_fault()
+        peers.close()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -277,6 +365,12 @@ def main():
         return 0
     if args.sweep:
         sweep()
+        return 0
+    if args.exchange_micro:
+        if world < 2:
+            print(json.dumps({"exchange_micro": "needs torchrun with 2 or more ranks"}))
+            return 0
+        exchange_micro()
         return 0
 
     # CPU baseline first (rank 0, N = 1): its spawn pool starts before any CUDA work.
@@ -322,7 +416,8 @@ def main():
         first.k, first.v, first.table = k_loc, v_loc, t_loc
         torch.cuda.empty_cache()
         cp = parallel.ContextParallelDecode(first.spec, device, kernel=args.kernel,
-                                            local_splits=args.splits or 0)
+                                            local_splits=args.splits or 0,
+                                            exchange=args.exchange)
         copies, wls = 1, [first]
         cp(first.q, k_loc, v_loc, t_loc, first.lengths)
         plan = cp.plan
@@ -480,7 +575,10 @@ def main():
                        "head_dim": first.spec.head_dim, "context": first.spec.max_context_len,
                        "splits": plan.splits, "tokens_per_split": plan.tokens_per_split,
                        "kv_bytes_per_step": kv_bytes, "kernel": kernel_name,
-                       "parallelism": (f"context-parallel x{world} (NCCL all-gather + LSE merge)"
+                       "parallelism": (f"context-parallel x{world} ("
+                                       + ("one peer-memory exchange kernel over NVLink"
+                                          if args.exchange == "p2p" else
+                                          "NCCL all-gather + LSE merge") + ")"
                                        if context else f"batch-sharded x{world}" if world > 1
                                        else "single GPU"),
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",
@@ -497,12 +595,16 @@ def main():
                     "d2h_bytes_per_step": d2h, "us_per_call": round(e2e_ms / K * 1e3, 3),
                     "api": ("paged_decode.parallel.ContextParallelDecode" if context
                             else "paged_decode.matched_splitkv.matched_decode")},
-            "gpu_launches": (5 if context else 2) * K * reps,
+            # Own kernels per step: partition + merge; context mode adds the
+            # local merge (nccl) or replaces both merges by the exchange (p2p).
+            "gpu_launches": ((3 if args.exchange == "nccl" else 2) if context else 2) * K * reps,
             "clocks": clocks.summary(windows),
             "fault_word": fault,
         }
         print(json.dumps(line), flush=True)
     del step_graph, part_graph
+    if context:
+        cp.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

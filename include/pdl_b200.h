@@ -11,11 +11,12 @@
  * KV head h / (num_heads / num_kv_heads).  Table entries past
  * ceil(lengths[b] / 256) are padding (may be -1) and are never read.
  *
- * All entry points take raw device pointers and sizes, enqueue work on the
- * given stream, never allocate, never synchronise and never read device
+ * All launch entry points take raw device pointers and sizes, enqueue work on
+ * the given stream, never allocate, never synchronise and never read device
  * memory from the host, so they may be captured in a CUDA graph (warm up
- * once per device/geometry before capture).  They return PDL_OK or a
- * PdlStatus; no C++ exception crosses this boundary.
+ * once per device/geometry before capture).  The pdl_peer_buffer_* set-up
+ * calls are the exception: they allocate, map and synchronise.  Every entry
+ * point returns PDL_OK or a PdlStatus; no C++ exception crosses this boundary.
  */
 #ifndef PDL_B200_H
 #define PDL_B200_H
@@ -29,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st *pdl_stream_t; /* same handle as cudaStream_t */
 
-#define PDL_ABI_VERSION 2
+#define PDL_ABI_VERSION 3
 #define PDL_PAGE_SIZE 256
 
 typedef enum PdlStatus {
@@ -249,6 +250,79 @@ typedef struct PdlAppendArgs {
  * loop can be captured in a CUDA graph.  Slots outside the pool and rows
  * whose table is full are skipped. */
 int pdl_append_kv(const PdlAppendArgs *args, pdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Context-parallel combine over peer memory (no counterpart in the
+ * reference, which has no multi-GPU path).  One process per GPU; every rank
+ * owns one exchange buffer, created with pdl_peer_buffer_create and mapped
+ * into every other rank's process with pdl_peer_buffer_open (CUDA IPC; the
+ * 64-byte handles travel over the host process group).  pdl_exchange_merge
+ * then replaces "local merge -> all-gather -> merge" with ONE kernel: each
+ * rank merges its local partitions, stores the merged FP32 partial + LSE
+ * into every rank's buffer over NVLink, each value tagged with the call's
+ * sequence number, waits (bounded) until every rank's values of its rows
+ * carry that sequence and merges the `world` blocks into its BF16 output.
+ * Output bits equal the two-kernel path's.
+ * ---------------------------------------------------------------------- */
+#define PDL_MAX_PEERS 8
+
+typedef struct PdlIpcHandle {
+  unsigned char bytes[64];    /* cudaIpcMemHandle_t */
+} PdlIpcHandle;
+
+/* Geometry of the exchange for `rows` (= batch * num_heads) rows. */
+typedef struct PdlExchangePlan {
+  int32_t ctas;               /* CTAs per rank (identical on identical GPUs)   */
+  int32_t reserved;
+  int64_t block_words;        /* 8-byte words per rank block: rows*D partials, rows LSEs
+                               * padded to an even count (value | sequence << 32)    */
+  int64_t data_offset;        /* bytes of per-warp sequence words before the data   */
+  int64_t buffer_bytes;       /* bytes each rank's exchange buffer needs        */
+} PdlExchangePlan;
+
+/* Pure arithmetic (no device access).  emulate_ranks: plan the single-GPU
+ * emulation launch of pdl_exchange_merge instead. */
+int pdl_exchange_plan(int32_t rows, int32_t head_dim, int32_t world, int32_t sm_count,
+                      int32_t emulate_ranks, PdlExchangePlan *plan);
+
+/* Allocate `bytes` of zeroed device memory on the current device (synchronises)
+ * and, if `handle` is not NULL, export it for other processes. */
+int pdl_peer_buffer_create(int64_t bytes, void **dev_ptr, PdlIpcHandle *handle);
+/* Map another process's buffer into this one (peer access over NVLink). */
+int pdl_peer_buffer_open(const PdlIpcHandle *handle, void **dev_ptr);
+/* Unmap a buffer opened with pdl_peer_buffer_open. */
+int pdl_peer_buffer_close(void *dev_ptr);
+/* Free a buffer made by pdl_peer_buffer_create (after every peer closed it). */
+int pdl_peer_buffer_free(void *dev_ptr);
+
+typedef struct PdlExchangeArgs {
+  const float *partial;       /* f32 [rows, parts, head_dim]: this rank's split workspace */
+  const float *lse;           /* f32 [rows, parts]                                        */
+  const int32_t *lengths;     /* optional int32 [rows / num_heads] tokens of each row in this
+                               * rank's range: only ceil(len / tokens_per_split) partitions
+                               * are read; NULL reads all `parts`                         */
+  int32_t num_heads;
+  int32_t tokens_per_split;
+  int32_t rows;
+  int32_t parts;
+  int32_t head_dim;
+  int32_t rank;
+  int32_t world;              /* 1 .. PDL_MAX_PEERS                                       */
+  /* 1: ONE cooperative launch on this GPU runs all `world` ranks (testing):
+   * partial, lse, lengths and out then hold `world` consecutive rank slices
+   * and every buffer is local.  `rank` is ignored. */
+  int32_t emulate_ranks;
+  uint32_t timeout_us;        /* bound on the wait for peers; 0 = 1 s, at most 10 s      */
+  void *buffers[PDL_MAX_PEERS]; /* rank q's exchange buffer as mapped here (buffer_bytes) */
+  void *out;                  /* bf16 [rows, head_dim]                                    */
+} PdlExchangeArgs;
+
+/* Every rank must call this with the same rows/parts/head_dim/world, in the
+ * same order as its other exchanges on the same buffers.  A wait that runs
+ * out sets a bit (16) in the fault word (pdl_read_fault) and leaves the
+ * waiting warp's remaining output rows unwritten; the buffers are then out
+ * of step and must be re-created on every rank. */
+int pdl_exchange_merge(const PdlExchangeArgs *args, pdl_stream_t stream);
 
 /* Static plan for `spec` on `sm_count` SMs; num_splits 0 = heuristic.
  * Replaces make_splitkv_plan (reference src/paged_decode/splitkv_plan.py:26-56). */

@@ -508,6 +508,123 @@ extern "C" int pdl_lse_merge(const PdlMergeArgs *args, pdl_stream_t stream) {
                           "lse merge");
 }
 
+// ---------------------------------------------------------------------------
+// Peer exchange (context-parallel combine).
+
+extern "C" int pdl_exchange_plan(int32_t rows, int32_t head_dim, int32_t world, int32_t sm_count,
+                                 int32_t emulate_ranks, PdlExchangePlan *plan) {
+  using namespace pdl;
+  if (plan == nullptr) return PDL_ERR_NULL;
+  if (!valid_dim(head_dim)) return fail(PDL_ERR_GEOMETRY, "exchange plan", "head_dim must be 64, 128 or 256");
+  if (rows <= 0 || sm_count <= 0) return fail(PDL_ERR_SHAPE, "exchange plan", "rows and sm_count must be positive");
+  if (world < 1 || world > PDL_MAX_PEERS) return fail(PDL_ERR_SHAPE, "exchange plan", "world must be 1..8");
+  static_assert(PDL_MAX_PEERS == kMaxPeers, "peer limit mismatch");
+  std::memset(plan, 0, sizeof(*plan));
+  plan->ctas = exchange_ctas(rows, head_dim, world, sm_count, emulate_ranks != 0);
+  plan->block_words = (int64_t)rows * head_dim + 2 * (((int64_t)rows + 1) / 2);
+  plan->data_offset = kExchangeHeaderBytes;
+  plan->buffer_bytes = kExchangeHeaderBytes + 2 * (int64_t)world * plan->block_words * 8;
+  return PDL_OK;
+}
+
+extern "C" int pdl_peer_buffer_create(int64_t bytes, void **dev_ptr, PdlIpcHandle *handle) {
+  using namespace pdl;
+  if (dev_ptr == nullptr) return PDL_ERR_NULL;
+  if (bytes <= 0) return fail(PDL_ERR_SHAPE, "peer buffer", "size must be positive");
+  *dev_ptr = nullptr;
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return cuda_fail("cudaMalloc(peer buffer)", e);
+  e = cudaMemset(p, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess && handle != nullptr) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(PdlIpcHandle), "IPC handle size");
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) std::memcpy(handle->bytes, &h, sizeof(h));
+  }
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail("peer buffer set-up", e);
+  }
+  *dev_ptr = p;
+  return PDL_OK;
+}
+
+extern "C" int pdl_peer_buffer_open(const PdlIpcHandle *handle, void **dev_ptr) {
+  using namespace pdl;
+  if (handle == nullptr || dev_ptr == nullptr) return PDL_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  void *p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail("cudaIpcOpenMemHandle", e);
+  *dev_ptr = p;
+  return PDL_OK;
+}
+
+extern "C" int pdl_peer_buffer_close(void *dev_ptr) {
+  using namespace pdl;
+  if (dev_ptr == nullptr) return PDL_ERR_NULL;
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? PDL_OK : cuda_fail("cudaIpcCloseMemHandle", e);
+}
+
+extern "C" int pdl_peer_buffer_free(void *dev_ptr) {
+  using namespace pdl;
+  if (dev_ptr == nullptr) return PDL_ERR_NULL;
+  const cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? PDL_OK : cuda_fail("cudaFree(peer buffer)", e);
+}
+
+extern "C" int pdl_exchange_merge(const PdlExchangeArgs *args, pdl_stream_t stream) {
+  using namespace pdl;
+  if (args == nullptr || args->partial == nullptr || args->lse == nullptr || args->out == nullptr)
+    return PDL_ERR_NULL;
+  const PdlExchangeArgs &a = *args;
+  if (!valid_dim(a.head_dim)) return fail(PDL_ERR_GEOMETRY, "exchange", "head_dim must be 64, 128 or 256");
+  if (a.rows <= 0 || a.parts <= 0) return fail(PDL_ERR_SHAPE, "exchange", "rows and parts must be positive");
+  if (a.world < 1 || a.world > PDL_MAX_PEERS) return fail(PDL_ERR_SHAPE, "exchange", "world must be 1..8");
+  if (!a.emulate_ranks && (a.rank < 0 || a.rank >= a.world))
+    return fail(PDL_ERR_SHAPE, "exchange", "rank outside [0, world)");
+  for (int q = 0; q < a.world; ++q) {
+    if (a.buffers[q] == nullptr) return fail(PDL_ERR_NULL, "exchange", "missing peer buffer");
+    if (!aligned(a.buffers[q], 256)) return fail(PDL_ERR_ALIGNMENT, "exchange", "peer buffer not 256-byte aligned");
+  }
+  if (a.lengths != nullptr &&
+      (a.num_heads <= 0 || a.rows % a.num_heads != 0 || a.tokens_per_split <= 0))
+    return fail(PDL_ERR_SHAPE, "exchange", "lengths need num_heads dividing rows and tokens_per_split > 0");
+  if (!aligned(a.partial, 16) || !aligned(a.out, 16))
+    return fail(PDL_ERR_ALIGNMENT, "exchange", "partial and out must be 16-byte aligned");
+  if (a.timeout_us > 10u * 1000u * 1000u) return fail(PDL_ERR_SHAPE, "exchange", "timeout above 10 s");
+  DeviceState *dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != PDL_OK) return st;
+  PdlExchangePlan plan;
+  st = pdl_exchange_plan(a.rows, a.head_dim, a.world, dev->sm_count, a.emulate_ranks, &plan);
+  if (st != PDL_OK) return st;
+  ExchangeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.partial = a.partial;
+  p.lse = a.lse;
+  p.lengths = a.lengths;
+  p.num_heads = a.lengths != nullptr ? a.num_heads : 1;
+  p.tokens_per_split = a.lengths != nullptr ? a.tokens_per_split : 1;
+  p.rows = a.rows;
+  p.splits = a.parts;
+  p.rank = a.emulate_ranks ? 0 : a.rank;
+  p.world = a.world;
+  p.emulate = a.emulate_ranks ? 1 : 0;
+  p.ctas = plan.ctas;
+  p.block = plan.block_words;
+  for (int q = 0; q < a.world; ++q) p.buffers[q] = static_cast<unsigned char *>(a.buffers[q]);
+  p.out = static_cast<__nv_bfloat16 *>(a.out);
+  p.timeout_ns = (uint64_t)(a.timeout_us ? a.timeout_us : 1000u * 1000u) * 1000ull;
+  p.fault = dev->fault;
+  return status_from_cuda(launch_exchange(p, a.head_dim, reinterpret_cast<cudaStream_t>(stream)),
+                          "exchange merge");
+}
+
 extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) {
   int st = validate_common(args);
   if (st == PDL_OK) st = validate_partition_inputs(args);

@@ -22,6 +22,7 @@ enum FaultBits : uint32_t {
   FAULT_CONSUMER_FULL_WAIT = 1u << 1,   // consumer gave up waiting for a TMA tile
   FAULT_DRAIN_WAIT = 1u << 2,           // in-flight copies did not land at exit
   FAULT_SMEM_ALIGN = 1u << 3,           // dynamic shared memory not 1024-byte aligned
+  FAULT_EXCHANGE_WAIT = 1u << 4,        // a peer's exchange flag did not arrive in time
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

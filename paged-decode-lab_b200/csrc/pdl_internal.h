@@ -97,6 +97,44 @@ struct AppendParams {
 
 cudaError_t launch_append(const AppendParams &params, cudaStream_t stream);
 
+// Peer exchange of the context-parallel merge (pdl_exchange.cu).
+// Every rank's exchange buffer has the same layout:
+//   uint32 seq[kMaxExchangeWarps]    calls completed by warp w of this rank (local only)
+//   uint64 data[2][world][block]     at kExchangeHeaderBytes; half = sequence & 1
+// where a rank block holds rows*D merged partial words, then rows LSE words
+// (padded to an even count).  A word is (float bits) | (sequence << 32):
+// the reader knows a value is current when its sequence matches.
+constexpr int kMaxPeers = 8;
+constexpr int kMaxExchangeCtas = 1024;
+constexpr int kExchangeWarps = 4;  // warps per exchange CTA
+constexpr int kMaxExchangeWarps = kMaxExchangeCtas * kExchangeWarps;
+constexpr int64_t kExchangeHeaderBytes = int64_t(kMaxExchangeWarps) * 4;
+constexpr int kExchangeCtasPerSm = 4;  // occupancy the exchange kernel is built for
+
+struct ExchangeParams {
+  const float *partial;     // [rows, splits, D] local split workspace (LSE protocol)
+  const float *lse;         // [rows, splits]
+  const int32_t *lengths;   // optional local lengths [rows / num_heads]
+  int32_t num_heads;
+  int32_t tokens_per_split;
+  int32_t rows;
+  int32_t splits;
+  int32_t rank;
+  int32_t world;
+  int32_t emulate;          // 1: blockIdx.y is the rank, every rank's slices and buffers on this GPU
+  int32_t ctas;             // CTAs per rank; the same on every rank
+  int64_t block;            // 8-byte words per rank block
+  unsigned char *buffers[kMaxPeers];
+  __nv_bfloat16 *out;       // [rows, D]
+  uint64_t timeout_ns;
+  uint32_t *fault;
+};
+
+cudaError_t launch_exchange(const ExchangeParams &params, int head_dim, cudaStream_t stream);
+// CTAs per rank of an exchange launch (a function of the shape and SM count
+// only, so every rank of a node computes the same grid).
+int exchange_ctas(int rows, int head_dim, int world, int sm_count, bool emulate);
+
 struct KernelLaunch {
   const CUtensorMap *k_map;
   const CUtensorMap *v_map;

@@ -12,61 +12,19 @@
 // the same kernel merges the split workspace ([B,Hq,S,D], S contiguous) and
 // the rank-major buffer an all-gather produces ([N][B*Hq][D]).
 //
-// LSE protocol (reference src/paged_decode/matched_splitkv.py:101-127):
-//   M = max_p lse_p (an all -inf row uses 0); total = sum_p exp(lse_p - M);
-//   logsum = ln(total) + M, or +inf when total = 0;
-//   out = sum_p exp(lse_p - logsum) * partial_p.
-// Optionally the merged row is stored as an FP32 partial plus its LSE
-// (logsum, or -inf for an empty row), so a merge can feed another merge.
-// MLA protocol (reference src/paged_decode/kernels.py:83-100):
-//   M = max_p m_p (-inf -> 0); f_p = exp(m_p - M);
-//   out = sum_p f_p * acc_p / (sum_p f_p * l_p, or 1 when that is 0).
+// The arithmetic (LSE and MLA protocols) is merge_slice in
+// pdl_merge_core.cuh.  Optionally the merged row is stored as an FP32
+// partial plus its LSE (logsum, or -inf for an empty row), so a merge can
+// feed another merge.
 // When `lengths` is given, only the ceil(len / tokens_per_split) live
 // partitions of a row are read (the others hold no tokens and their weights
 // are exactly 0), so empty partitions need not be stored at all.
-#include "pdl_device.cuh"
+#include "pdl_merge_core.cuh"
 
 namespace pdl {
 namespace {
 
 constexpr int MERGE_WARPS = 4;
-
-template <int E>
-__device__ __forceinline__ void load_cols(const float *src, float (&v)[E]) {
-  if constexpr (E == 2) {
-    const float2 a = *reinterpret_cast<const float2 *>(src);
-    v[0] = a.x; v[1] = a.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < E; i += 4) {
-      const float4 a = *reinterpret_cast<const float4 *>(src + i);
-      v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
-    }
-  }
-}
-
-template <int E>
-__device__ __forceinline__ void store_cols(float *dst, const float (&v)[E]) {
-  if constexpr (E == 2) {
-    *reinterpret_cast<float2 *>(dst) = make_float2(v[0], v[1]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < E; i += 4)
-      *reinterpret_cast<float4 *>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-  }
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL_MASK, v, o));
-  return v;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);
-  return v;
-}
 
 template <int D>
 __global__ void __launch_bounds__(32 * MERGE_WARPS)
@@ -89,70 +47,10 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
   const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;
-
-  // Weights of partitions lane, lane+32, ... stay in registers (up to 128
-  // partitions; more are re-read).
-  constexpr int WR = 4;
-  float wreg[WR];
-#pragma unroll
-  for (int i = 0; i < WR; ++i)
-    wreg[i] = lane + 32 * i < live ? __ldcg(w_src + (lane + 32 * i) * p.w_part_stride) : -INFINITY;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < WR; ++i) mx = fmaxf(mx, wreg[i]);
-  for (int s = lane + 32 * WR; s < live; s += 32) mx = fmaxf(mx, __ldcg(w_src + s * p.w_part_stride));
-  mx = warp_max(mx);
-  if (mx == -INFINITY) mx = 0.f;
-
-  float shift = mx;   // exponent subtracted from every weight
-  float scale = 1.f;  // final multiplier
-  float tot = 0.f;
-  if (lse_protocol) {
-#pragma unroll
-    for (int i = 0; i < WR; ++i) tot += lane + 32 * i < live ? expf(wreg[i] - mx) : 0.f;
-    for (int s = lane + 32 * WR; s < live; s += 32) tot += expf(__ldcg(w_src + s * p.w_part_stride) - mx);
-    tot = warp_sum(tot);
-    shift = tot > 0.f ? logf(tot) + mx : INFINITY;
-  } else {
-    const float *l_src = p.denoms + (int64_t)row * p.w_row_stride;
-    for (int s = lane; s < live; s += 32)
-      tot += __ldcg(l_src + s * p.w_part_stride) * expf(__ldcg(w_src + s * p.w_part_stride) - mx);
-    tot = warp_sum(tot);
-    scale = 1.f / (tot > 0.f ? tot : 1.f);
-  }
-
-  float acc[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int s0 = 0; s0 < live; s0 += 32) {
-    const int wi = s0 / 32;
-    // Register select (a dynamic index would put wreg in local memory).
-    const float wsrc = wi == 0 ? wreg[0] : wi == 1 ? wreg[1] : wi == 2 ? wreg[2]
-                     : wi == 3 ? wreg[3]
-                     : (s0 + lane < live ? __ldcg(w_src + (s0 + lane) * p.w_part_stride)
-                                         : -INFINITY);
-    const float wl = (s0 + lane < live) ? expf(wsrc - shift) : 0.f;
-    const int n = min(32, live - s0);
-    // Rows of up to BATCH partitions are loaded before any is consumed, so
-    // the memory round trips overlap instead of serialising per partition.
-    constexpr int BATCH = E <= 4 ? 16 : 8;
-    for (int k0 = 0; k0 < n; k0 += BATCH) {
-      float v[BATCH][E];
-#pragma unroll
-      for (int j = 0; j < BATCH; ++j)
-        load_cols<E>(r_src + (int64_t)(s0 + min(k0 + j, n - 1)) * p.part_stride + lane * E, v[j]);
-#pragma unroll
-      for (int j = 0; j < BATCH; ++j) {
-        const float wk = __shfl_sync(FULL_MASK, wl, min(k0 + j, 31));
-        if (k0 + j < n) {
-#pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[j][e], acc[e]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] *= scale;
+  const float *l_src = lse_protocol ? nullptr : p.denoms + (int64_t)row * p.w_row_stride;
+  float acc[E], shift, tot;
+  merge_slice<E, (E <= 4 ? 16 : 8), false>(lse_protocol, w_src, p.w_part_stride, l_src, r_src,
+                                          p.part_stride, live, lane, acc, shift, tot);
   if (p.out != nullptr) {
     __nv_bfloat16 *dst = p.out + (int64_t)row * D + col0 + lane * E;
 #pragma unroll
@@ -160,7 +58,7 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
       *reinterpret_cast<__nv_bfloat162 *>(dst + e) = __floats2bfloat162_rn(acc[e], acc[e + 1]);
   }
   if (p.out_partial != nullptr)
-    store_cols<E>(p.out_partial + (int64_t)row * D + col0 + lane * E, acc);
+    merge_store_cols<E>(p.out_partial + (int64_t)row * D + col0 + lane * E, acc);
   if (p.out_lse != nullptr && lane == 0 && col0 == 0)
     p.out_lse[row] = tot > 0.f ? shift : -INFINITY;
 }

@@ -8,7 +8,7 @@ import ctypes
 from pathlib import Path
 
 LIBRARY = Path(__file__).with_name("libpdl_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 PDL_OK = 0
 STATUS_NAMES = {
@@ -23,9 +23,13 @@ FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE, FLAG_DYNAMIC = 1, 2, 4, 8
 # Every extern "C" symbol declared in include/pdl_b200.h.
 SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode", "pdl_append_kv",
            "pdl_paged_decode_static_scratch", "pdl_splitkv_plan", "pdl_b200_plan",
-           "pdl_spec_geometry",
+           "pdl_spec_geometry", "pdl_exchange_plan", "pdl_peer_buffer_create",
+           "pdl_peer_buffer_open", "pdl_peer_buffer_close", "pdl_peer_buffer_free",
+           "pdl_exchange_merge",
            "pdl_status_string", "pdl_last_error", "pdl_abi_version", "pdl_read_fault")
 STATIC_SCRATCH_BYTES = 4 << 20
+MAX_PEERS = 8
+FAULT_EXCHANGE_WAIT = 1 << 4
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -70,6 +74,22 @@ class PdlMergeArgs(ctypes.Structure):
                 ("out_lse", _vp)]
 
 
+class PdlIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class PdlExchangePlan(ctypes.Structure):
+    _fields_ = [("ctas", _i32), ("reserved", _i32), ("block_words", _i64),
+                ("data_offset", _i64), ("buffer_bytes", _i64)]
+
+
+class PdlExchangeArgs(ctypes.Structure):
+    _fields_ = [("partial", _vp), ("lse", _vp), ("lengths", _vp), ("num_heads", _i32),
+                ("tokens_per_split", _i32), ("rows", _i32), ("parts", _i32),
+                ("head_dim", _i32), ("rank", _i32), ("world", _i32), ("emulate_ranks", _i32),
+                ("timeout_us", ctypes.c_uint32), ("buffers", _vp * 8), ("out", _vp)]
+
+
 _LIB = None
 
 
@@ -100,6 +120,18 @@ def load():
     lib.pdl_spec_geometry.argtypes = [ctypes.POINTER(PdlSpec), ctypes.POINTER(_i32),
                                       ctypes.POINTER(_i32), ctypes.POINTER(_i64)]
     lib.pdl_spec_geometry.restype = ctypes.c_int
+    lib.pdl_exchange_plan.argtypes = [_i32, _i32, _i32, _i32, _i32,
+                                      ctypes.POINTER(PdlExchangePlan)]
+    lib.pdl_exchange_plan.restype = ctypes.c_int
+    lib.pdl_peer_buffer_create.argtypes = [_i64, ctypes.POINTER(_vp), ctypes.POINTER(PdlIpcHandle)]
+    lib.pdl_peer_buffer_create.restype = ctypes.c_int
+    lib.pdl_peer_buffer_open.argtypes = [ctypes.POINTER(PdlIpcHandle), ctypes.POINTER(_vp)]
+    lib.pdl_peer_buffer_open.restype = ctypes.c_int
+    for name in ("pdl_peer_buffer_close", "pdl_peer_buffer_free"):
+        getattr(lib, name).argtypes = [_vp]
+        getattr(lib, name).restype = ctypes.c_int
+    lib.pdl_exchange_merge.argtypes = [ctypes.POINTER(PdlExchangeArgs), ctypes.c_size_t]
+    lib.pdl_exchange_merge.restype = ctypes.c_int
     lib.pdl_status_string.argtypes = [ctypes.c_int]
     lib.pdl_status_string.restype = ctypes.c_char_p
     lib.pdl_last_error.argtypes = []

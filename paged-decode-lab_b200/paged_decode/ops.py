@@ -163,3 +163,82 @@ def read_fault(clear=False):
 
 def sm_count(device):
     return torch.cuda.get_device_properties(torch.device(device)).multi_processor_count
+
+
+# ------------------------------------------------------------ peer exchange
+def exchange_plan(rows, head_dim, world, sm_count, emulate=False):
+    """``pdl_exchange_plan``: CTAs per rank, rank-block floats, buffer bytes."""
+    plan = _lib.PdlExchangePlan()
+    status = _lib.load().pdl_exchange_plan(int(rows), int(head_dim), int(world), int(sm_count),
+                                           int(bool(emulate)), ctypes.byref(plan))
+    if status != _lib.PDL_OK:
+        raise ValueError(f"invalid exchange plan request: {_lib.status_text(status)}")
+    return plan
+
+
+def _on_device(device, fn):
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    with torch.cuda.device(index):
+        return fn()
+
+
+class PeerBuffer:
+    """Zeroed device memory owned by this process, exportable over CUDA IPC."""
+
+    def __init__(self, nbytes, device):
+        self.device = torch.device(device)
+        self.nbytes = int(nbytes)
+        ptr, handle = ctypes.c_void_p(), _lib.PdlIpcHandle()
+        status = _on_device(self.device, lambda: _lib.load().pdl_peer_buffer_create(
+            self.nbytes, ctypes.byref(ptr), ctypes.byref(handle)))
+        if status != _lib.PDL_OK:
+            raise RuntimeError(f"pdl_peer_buffer_create failed: {_lib.status_text(status)}")
+        self.ptr = ptr.value
+        self.handle = bytes(handle.bytes)
+
+    def free(self):
+        if self.ptr:
+            ptr, self.ptr = self.ptr, None
+            status = _on_device(self.device, lambda: _lib.load().pdl_peer_buffer_free(ptr))
+            if status != _lib.PDL_OK:
+                raise RuntimeError(f"pdl_peer_buffer_free failed: {_lib.status_text(status)}")
+
+
+def open_peer_buffer(handle, device):
+    """Map another process's PeerBuffer (64-byte handle) into this one."""
+    h = _lib.PdlIpcHandle()
+    ctypes.memmove(h.bytes, bytes(handle), 64)
+    ptr = ctypes.c_void_p()
+    status = _on_device(torch.device(device), lambda: _lib.load().pdl_peer_buffer_open(
+        ctypes.byref(h), ctypes.byref(ptr)))
+    if status != _lib.PDL_OK:
+        raise RuntimeError(f"pdl_peer_buffer_open failed: {_lib.status_text(status)}")
+    return ptr.value
+
+
+def close_peer_buffer(ptr, device):
+    status = _on_device(torch.device(device), lambda: _lib.load().pdl_peer_buffer_close(ptr))
+    if status != _lib.PDL_OK:
+        raise RuntimeError(f"pdl_peer_buffer_close failed: {_lib.status_text(status)}")
+
+
+def exchange_args(partial, lse, *, rows, parts, head_dim, world, buffers, out, rank=0,
+                  lengths=None, num_heads=0, tokens_per_split=0, emulate=False, timeout_us=0):
+    """Fill a ``PdlExchangeArgs``; ``buffers`` are raw device addresses (one per rank)."""
+    if len(buffers) != world or world > _lib.MAX_PEERS:
+        raise ValueError("one exchange buffer per rank, at most 8 ranks")
+    a = _lib.PdlExchangeArgs()
+    a.partial, a.lse, a.lengths = partial.data_ptr(), lse.data_ptr(), _addr(lengths)
+    a.num_heads, a.tokens_per_split = int(num_heads), int(tokens_per_split)
+    a.rows, a.parts, a.head_dim = int(rows), int(parts), int(head_dim)
+    a.rank, a.world, a.emulate_ranks = int(rank), int(world), int(bool(emulate))
+    a.timeout_us = int(timeout_us)
+    for q, ptr in enumerate(buffers):
+        a.buffers[q] = int(ptr)
+    a.out = out.data_ptr()
+    return a
+
+
+def exchange_merge(args, device):
+    """Local merge + peer exchange + merge in one kernel (``pdl_exchange_merge``)."""
+    _call("pdl_exchange_merge", args, device)

@@ -11,9 +11,12 @@ Three ways to spread one decode step over N GPUs of a node:
   tensor-parallel output projection expects.
 * context parallel -- for very long rows, rank r owns the pages
   [r*W/N, (r+1)*W/N) of every row (page aligned).  Each rank decodes its token
-  range to a normalised FP32 partial + LSE per (row, head), one NCCL
-  all-gather moves those (rows*(D+1) floats per rank), and every rank runs the
-  stable LSE merge over the N ranks.
+  range to a normalised FP32 partial + LSE per (row, head); those
+  (rows*(D+1) floats per rank) are exchanged and every rank runs the stable
+  LSE merge over the N ranks.  The exchange is either one NCCL all-gather
+  between a local and a global merge kernel, or (``exchange="p2p"``) one
+  kernel that stores the local merge into every peer's buffer over NVLink
+  and merges after a bounded flag wait (``PeerExchange``).
 
 The reference has no multi-GPU attention path; the planning functions are
 pure (no CUDA) so CPU process groups (gloo) can test them.
@@ -104,7 +107,86 @@ def exchange(send, gathered, group=None):
     dist.all_gather_into_tensor(gathered, send, group=group)
 
 
+def share_handles(handle, ctas, group=None, device=None):
+    """All-gather every rank's (64-byte IPC handle, planned CTA count).
+
+    Travels as one uint8 tensor per rank: on ``device`` for NCCL groups, on
+    the CPU otherwise.  Returns ``[(handle bytes, ctas)]`` indexed by rank.
+    """
+    if len(handle) != 64:
+        raise ValueError("CUDA IPC handles are 64 bytes")
+    world = dist.get_world_size(group)
+    on = torch.device(device) if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    mine = torch.tensor(list(handle) + list(int(ctas).to_bytes(4, "little")),
+                        dtype=torch.uint8, device=on)
+    every = torch.empty(world * mine.numel(), dtype=torch.uint8, device=on)
+    dist.all_gather_into_tensor(every, mine, group=group)
+    rows = every.view(world, -1).cpu().tolist()
+    return [(bytes(r[:64]), int.from_bytes(bytes(r[64:]), "little")) for r in rows]
+
+
 # ---------------------------------------------------------------- GPU decoders
+class PeerExchange:
+    """Exchange buffers of a process group for ``pdl_exchange_merge``.
+
+    Every rank creates one zeroed buffer (``PeerBuffer``) sized by
+    ``pdl_exchange_plan``; the 64-byte CUDA IPC handles and the planned CTA
+    count are all-gathered over ``group`` (on the GPU for NCCL groups), every
+    rank maps the others' buffers, and a barrier makes sure all mappings
+    exist before the first exchange.  ``ptrs[q]`` is rank q's buffer as seen
+    from this process.  Call ``close`` on every rank (it synchronises).
+    """
+
+    def __init__(self, rows, head_dim, device, group=None):
+        from . import ops
+        self.ops = ops
+        self.group = group
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.plan = ops.exchange_plan(rows, head_dim, self.world, ops.sm_count(self.device))
+        self.own = ops.PeerBuffer(self.plan.buffer_bytes, self.device)
+        try:
+            shared = share_handles(self.own.handle, self.plan.ctas, group, self.device)
+        except Exception:
+            self.own.free()
+            raise
+        ctas = [c for _, c in shared]
+        if len(set(ctas)) != 1:
+            self.own.free()
+            raise RuntimeError(f"ranks planned different exchange grids {ctas}; "
+                               "context parallelism needs identical GPUs")
+        self.ptrs = []
+        try:
+            for q in range(self.world):
+                self.ptrs.append(self.own.ptr if q == self.rank else
+                                 ops.open_peer_buffer(shared[q][0], self.device))
+        except Exception:
+            self._release()
+            raise
+        dist.barrier(group)
+
+    def _release(self):
+        for q, ptr in enumerate(self.ptrs):
+            if q != self.rank:
+                self.ops.close_peer_buffer(ptr, self.device)
+        self.ptrs = []
+        self.own.free()
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after every rank is done)."""
+        if self.own.ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        for q, ptr in enumerate(self.ptrs):
+            if q != self.rank:
+                self.ops.close_peer_buffer(ptr, self.device)
+        self.ptrs = []
+        dist.barrier(self.group)
+        self.own.free()
+
+
 class ContextParallelDecode:
     """Context-parallel decode of a long-row batch across the ranks of `group`.
 
@@ -114,10 +196,18 @@ class ContextParallelDecode:
     local lengths are derived on the device.  All buffers are allocated here,
     so the call itself (partition, local merge, all-gather, merge) can be
     captured in a CUDA graph.
+
+    ``exchange="nccl"``: partition, local merge, NCCL all-gather, merge (four
+    launches).  ``exchange="p2p"``: partition, then ``pdl_exchange_merge``
+    (two launches; needs every rank on its own GPU of one node with peer
+    access, and ``close()`` on every rank when done).  Both give the same bits.
     """
 
-    def __init__(self, spec, device, group=None, local_splits=0, kernel="auto"):
+    def __init__(self, spec, device, group=None, local_splits=0, kernel="auto",
+                 exchange="nccl"):
         """``local_splits`` 0 uses the B200 plan for the rank-local capacity."""
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
         from . import ops
         from .splitkv_plan import make_b200_plan, make_splitkv_plan
         self.ops = ops
@@ -144,7 +234,15 @@ class ContextParallelDecode:
         self.local_len = torch.zeros(b, device=self.device, dtype=torch.int32)
         # Dynamic-scheduler words of the local partition launch (left zeroed).
         self.counters = torch.zeros(b * hq + 2, device=self.device, dtype=torch.int32)
+        self.exchange_mode = exchange
+        self.peer = PeerExchange(b * hq, d, self.device, group) if exchange == "p2p" else None
         self._args = {}
+
+    def close(self):
+        """Release the peer-exchange buffers (p2p mode; call on every rank)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _launch_args(self, q, k_local, v_local, table_local, scale):
         ops = self.ops
@@ -157,6 +255,14 @@ class ContextParallelDecode:
                                    protocol=ops.PROTOCOL_LSE, kernel=self.kernel,
                                    partial=self.partials, lse=self.lse, counters=self.counters,
                                    flags=ops.FLAG_DYNAMIC)
+            if self.peer is not None:
+                ex = ops.exchange_args(self.partials, self.lse, rows=rows, parts=s, head_dim=d,
+                                       rank=self.rank, world=self.world, buffers=self.peer.ptrs,
+                                       out=self.out, lengths=self.local_len,
+                                       num_heads=self.spec.num_heads,
+                                       tokens_per_split=self.plan.tokens_per_split)
+                self._args[key] = (part, ex, None)
+                return self._args[key]
             send_p, send_l = self.layout.send_views(self.send)
             local = ops.merge_args(self.partials, self.lse, rows=rows, parts=s, head_dim=d,
                                    row_stride=s * d, part_stride=d, lse_row_stride=s,
@@ -176,6 +282,9 @@ class ContextParallelDecode:
         part, local, glob = self._launch_args(q, k_local, v_local, table_local, scale)
         local_lengths(lengths, self.rank, self.per_rank, out=self.local_len)
         self.ops.partition(part, self.device)
+        if glob is None:
+            self.ops.exchange_merge(local, self.device)
+            return self.out
         self.ops.lse_merge(local, self.device)
         exchange(self.send, self.gathered, self.group)
         self.ops.lse_merge(glob, self.device)

@@ -4,6 +4,9 @@ Every rank builds the same seeded global workload on its own GPU, computes
 the unsharded single-GPU result locally, then checks:
   * context parallel (local partial + LSE, one all-gather, LSE merge) against
     the single-GPU output, eager and replayed from a CUDA graph;
+  * the same with the peer-memory exchange (``exchange="p2p"``: one kernel
+    stores into every rank's IPC-mapped buffer and merges after a bounded
+    flag wait): bit-identical to the all-gather path, eager and in a graph;
   * batch sharding: its rows, decoded alone, equal the unsharded rows bit for bit;
   * KV-head sharding: its head slice equals the unsharded heads bit for bit.
 Rank 0 prints one JSON line with the results; any failure raises.
@@ -80,6 +83,32 @@ def main():
     report["context_graph_equals_eager"] = bool(torch.equal(eager, replayed))
     del graph
 
+    # ---- context parallel over peer memory (one exchange kernel)
+    p2p = parallel.ContextParallelDecode(spec, device, local_splits=0, exchange="p2p")
+    lens.copy_(torch.tensor([width * 256, 40_000], dtype=torch.int32, device=device))
+    nccl_out = cp(q, k_loc, v_loc, t_loc, lens).clone()
+    p2p_out = p2p(q, k_loc, v_loc, t_loc, lens).clone()
+    report["p2p_equals_nccl"] = bool(torch.equal(p2p_out, nccl_out))
+    with torch.cuda.stream(stream):
+        stream.wait_stream(torch.cuda.current_stream(device))
+        for _ in range(3):
+            p2p(q, k_loc, v_loc, t_loc, lens)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        p2p(q, k_loc, v_loc, t_loc, lens)
+    ok = True
+    for new_lens in ([12_345, width * 256 - 7], [0, 1], [width * 256, 256]):
+        lens.copy_(torch.tensor(new_lens, dtype=torch.int32, device=device))
+        graph.replay()
+        torch.cuda.synchronize(device)
+        ok &= bool(torch.equal(p2p.out, cp(q, k_loc, v_loc, t_loc, lens)))
+    report["p2p_graph_equals_nccl"] = ok
+    del graph
+    torch.cuda.synchronize(device)
+    report["p2p_fault_word"] = ops.read_fault()
+    p2p.close()
+
     # ---- batch sharding (variable lengths): rows decode independently
     b, hq, hkv, d, width = 16, 32, 8, 128, 32
     pages = b * width
@@ -103,7 +132,9 @@ def main():
     report["head_bit_exact"] = bool(torch.equal(mine, full[:, q_lo:q_hi]))
 
     flags = torch.tensor([report["context_eager_err"] <= TOL, report["context_graph_err"] <= TOL,
-                          report["context_graph_equals_eager"], report["batch_bit_exact"],
+                          report["context_graph_equals_eager"], report["p2p_equals_nccl"],
+                          report["p2p_graph_equals_nccl"], report["p2p_fault_word"] == 0,
+                          report["batch_bit_exact"],
                           report["head_bit_exact"]], device=device, dtype=torch.int32)
     dist.all_reduce(flags, op=dist.ReduceOp.MIN)
     report["all_ranks_ok"] = bool(flags.min().item())

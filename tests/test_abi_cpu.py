@@ -168,3 +168,48 @@ def test_b200_plan_invariants():
         assert (plan.splits - 1) * plan.tokens_per_split < capacity  # no always-empty partition
         assert plan.tokens_per_split <= max(4096, plan.tile_tokens)
     assert make_b200_plan(DecodeSpec(128, 32, 8, 128, 32768), 148).splits == 8
+
+
+def test_exchange_plan_arithmetic():
+    lib = _lib.load()
+
+    def plan(rows, d, world, sms=148, emulate=0):
+        p = _lib.PdlExchangePlan()
+        status = lib.pdl_exchange_plan(rows, d, world, sms, emulate, ctypes.byref(p))
+        return status, p
+
+    status, p = plan(128, 128, 2)  # config 5: B=2 x Hq=64 rows
+    assert status == 0 and p.ctas == 32
+    assert p.block_words == 128 * 128 + 128 and p.data_offset == 4096 * 4
+    assert p.buffer_bytes == p.data_offset + 2 * 2 * p.block_words * 8
+    status, p = plan(3, 64, 1)
+    assert status == 0 and p.ctas == 1 and p.block_words == 3 * 64 + 4
+    status, p = plan(16384, 256, 8)  # two column slices per row; 4 CTAs per SM at most
+    assert status == 0 and p.ctas == 4 * 148
+    status, p = plan(16384, 256, 8, emulate=1)  # every emulated rank co-resident
+    assert status == 0 and p.ctas == 4 * 148 // 8
+    status, p = plan(1 << 20, 64, 2, sms=1000)
+    assert status == 0 and p.ctas == 1024  # flag arrays hold 1024 CTAs
+    for bad in [(128, 96, 2), (0, 128, 2), (128, 128, 0), (128, 128, 9)]:
+        assert plan(*bad)[0] != 0
+    assert lib.pdl_exchange_plan(1, 64, 1, 148, 0, None) == 1
+
+
+def test_exchange_entry_points_reject_null_without_a_gpu():
+    lib = _lib.load()
+    assert lib.pdl_exchange_merge(None, 0) == 1
+    assert lib.pdl_peer_buffer_create(0, None, None) == 1
+    assert lib.pdl_peer_buffer_open(None, None) == 1
+    assert lib.pdl_peer_buffer_close(None) == 1
+    assert lib.pdl_peer_buffer_free(None) == 1
+
+
+def test_exchange_args_need_one_buffer_per_rank():
+    import torch
+    from paged_decode import ops
+    t = torch.zeros(8)
+    with pytest.raises(ValueError):
+        ops.exchange_args(t, t, rows=1, parts=1, head_dim=64, world=2, buffers=[0], out=t)
+    a = ops.exchange_args(t, t, rows=1, parts=1, head_dim=64, world=2, buffers=[256, 512],
+                          out=t, rank=1, timeout_us=5)
+    assert a.world == 2 and a.rank == 1 and list(a.buffers)[:2] == [256, 512]

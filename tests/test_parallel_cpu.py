@@ -186,3 +186,26 @@ def test_exchange_fails_instead_of_hanging_when_a_rank_dies():
                            start_method="spawn")
     assert result.get(1) == "raised"
     assert str(result.get(0, "")).startswith("error")
+
+
+def _handles_rank(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        result[rank] = parallel.share_handles(bytes([rank + 1]) * 64, 32)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_handles_reach_every_rank():
+    """The set-up collective of the p2p exchange: every rank learns every
+    rank's IPC handle and planned grid, in rank order."""
+    world = 2
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.start_processes(_handles_rank, args=(world, free_port(), result), nprocs=world,
+                       start_method="spawn")
+    expect = [(bytes([r + 1]) * 64, 32) for r in range(world)]
+    assert result[0] == expect and result[1] == expect
+    with pytest.raises(ValueError):
+        parallel.share_handles(b"short", 1)
