@@ -330,8 +330,9 @@ int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t num_splits,
                      PdlPlan *plan);
 
 /* Split plan for this library's persistent, dynamically scheduled kernels on
- * `sm_count` SMs: about one work item per CTA slot, items of at most 4096
- * tokens, partitions a multiple of the reference plan's tile.  No counterpart
+ * `sm_count` SMs (two CTA slots per SM): at most one wave of work items, or
+ * (head_dim <= 128, items longer than 1024 tokens) two full waves; items of
+ * at most 4096 tokens; partitions a multiple of the reference plan's tile.  No counterpart
  * in the reference (its plan, pdl_splitkv_plan, is tuned for one CTA per
  * partition on A100). */
 int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *plan);

@@ -439,7 +439,17 @@ extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *pla
   const int64_t blocks = (capacity + tile - 1) / tile;
   const int64_t groups = (int64_t)spec->max_batch * spec->num_kv_heads;
   const int64_t slots = 2LL * sm_count;
-  int64_t splits = std::max<int64_t>((slots + groups / 2) / groups, (capacity + 4095) / 4096);
+  // One wave of items at most (rounding up would leave a few items for a
+  // second wave that a handful of CTAs stream alone), and items of at most
+  // 4096 tokens so variable lengths balance under dynamic scheduling.
+  int64_t splits = std::max<int64_t>(std::max<int64_t>(slots / groups, 1), (capacity + 4095) / 4096);
+  // Up to D = 128 an item's fixed cost is small, so a partial wave of long
+  // items becomes two full waves of shorter ones (measured, B=2 x 8 KV heads
+  // x 64k tokens: 304 items of 3456 tokens 0.76 of copy bandwidth, 576 of
+  // 1920 tokens 1.01).  At D = 256 the per-item cost dominates (B=32: 256
+  // items 0.81, 384 items 0.78) and one wave stays.
+  if (spec->head_dim <= 128 && groups * splits < 2 * slots && capacity / splits > 1024)
+    splits = (2 * slots + groups - 1) / groups;
   splits = std::min<int64_t>(std::max<int64_t>(splits, 1), blocks);
   const int64_t tps = (blocks + splits - 1) / splits * tile;
   splits = (capacity + tps - 1) / tps;  // drop partitions that would always be empty

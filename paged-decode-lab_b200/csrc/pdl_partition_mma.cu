@@ -14,9 +14,13 @@
 //       the S^T accumulator registers with movmatrix.trans.  P is split into
 //       BF16 hi + lo parts (two MMAs) so P.V keeps FP32-level accuracy.
 //
-// Each consumer warp owns 16*MT rows of every T-token tile and its own
-// running (m, l, O); the warps are merged at the end of an item through
-// shared memory (combine_and_store).  Rows outside the partition or beyond
+// Consumer warps come in NG token groups of DS warps.  Each group owns 16*MT
+// rows of every T-token tile and its own running (m, l, O); at D = 256 the
+// two warps of a group (DS = 2) both compute the group's scores (identical
+// instructions on identical data, so identical m, l and P) and each keeps
+// the O columns of its half of D, halving the P.V work per warp without any
+// exchange between them.  The groups are merged at the end of an item
+// through shared memory (combine_and_store).  Rows outside the partition or beyond
 // the live length are masked: scores to -inf, V fragment halves to zero
 // (dead page slots may hold NaN).
 //
@@ -31,21 +35,25 @@ namespace {
 
 template <int D>
 struct MmaShape {
-  static constexpr int NC = D == 256 ? 2 : 4;                      // consumer warps
+  static constexpr int NG = D == 256 ? 2 : 4;                      // token groups
+  static constexpr int DS = D == 256 ? 2 : 1;                      // warps per group (D split)
+  static constexpr int NC = NG * DS;                               // consumer warps
   static constexpr int T = D == 64 ? 128 : (D == 128 ? 64 : 32);   // tokens per stage
-  static constexpr int TW = T / NC;                                // rows per warp per stage
+  static constexpr int TW = T / NG;                                // rows per group per stage
   static constexpr int MT = TW / 16;                               // 16-row MMA tiles per warp
   static constexpr int KS = D / 16;                                // 16-column slices of D
+  static constexpr int KSW = KS / DS;                              // slices of O per warp
   static constexpr int SUB_BYTES = T * 128;
   static constexpr int TILE_BYTES = T * D * 2;
   static constexpr int NTHREADS = 32 * (NC + 1);
 };
 
-// Stages: 3 when two CTAs still fit one SM, else 2.
+// Stages: 3 when two CTAs still fit one SM, else 2.  The combine area holds
+// one partial state per token group.
 template <int D, int GC>
 struct MmaStages {
-  static constexpr int NC = MmaShape<D>::NC, T = MmaShape<D>::T;
-  static constexpr int NS = PartitionSmem<D, T, 3, NC, GC>::BYTES <= kTwoCtaSmemBytes ? 3 : 2;
+  static constexpr int NG = MmaShape<D>::NG, T = MmaShape<D>::T;
+  static constexpr int NS = PartitionSmem<D, T, 3, NG, GC>::BYTES <= kTwoCtaSmemBytes ? 3 : 2;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -98,8 +106,9 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   using S = MmaShape<D>;
   constexpr int GC = 8 * NT;
   constexpr int NS = MmaStages<D, GC>::NS;
-  using L = PartitionSmem<D, S::T, NS, S::NC, GC>;
-  constexpr int NC = S::NC, T = S::T, TW = S::TW, MT = S::MT, KS = S::KS;
+  using L = PartitionSmem<D, S::T, NS, S::NG, GC>;
+  constexpr int NC = S::NC, NG = S::NG, DS = S::DS, T = S::T, TW = S::TW, MT = S::MT;
+  constexpr int KS = S::KS, KSW = S::KSW;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *kbuf = smem;
@@ -139,6 +148,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
 
   // -------------------------------------------------------------- consumers
   const int cw = warp - 1;
+  const int tg = cw / DS, dh = cw % DS;  // token group, half of D (DS = 2)
   const int tid = cw * 32 + lane;
   const int quad = lane & 3, grp = lane >> 2;  // MMA fragment coordinates
   // ldmatrix row providers: lane -> (matrix mi, row rr).
@@ -181,20 +191,20 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       continue;
     }
 
-    // Running state for heads nt*8 + quad*2 + {0,1}; acc[nt][dm] holds
-    // O^T rows dm*16 + grp (+8) for those two heads.
-    float m[NT][2], l[NT][2], acc[NT][KS][4];
+    // Running state for heads nt*8 + quad*2 + {0,1}; acc[nt][j] holds O^T
+    // rows (dh*KSW + j)*16 + grp (+8) for those two heads.
+    float m[NT][2], l[NT][2], acc[NT][KSW][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       m[nt][0] = m[nt][1] = -INFINITY;
       l[nt][0] = l[nt][1] = 0.f;
 #pragma unroll
-      for (int dm = 0; dm < KS; ++dm) acc[nt][dm][0] = acc[nt][dm][1] = acc[nt][dm][2] = acc[nt][dm][3] = 0.f;
+      for (int dm = 0; dm < KSW; ++dm) acc[nt][dm][0] = acc[nt][dm][1] = acc[nt][dm][2] = acc[nt][dm][3] = 0.f;
     }
 
     const int t0 = rg.start / T * T;
     const int ntiles = (rg.stop - t0 + T - 1) / T;
-    const int r0 = cw * TW;
+    const int r0 = tg * TW;
     for (int i = 0; i < ntiles; ++i, ++it) {
       const int s = it % NS;
       pipeline_wait(&full[s], (it / NS) & 1, p.fault, FAULT_CONSUMER_FULL_WAIT, abort_flag);
@@ -268,7 +278,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
             m[nt][j] = mn;
             l[nt][j] *= alpha;
 #pragma unroll
-            for (int dm = 0; dm < KS; ++dm) {
+            for (int dm = 0; dm < KSW; ++dm) {
               acc[nt][dm][j] *= alpha;
               acc[nt][dm][j + 2] *= alpha;
             }
@@ -295,11 +305,11 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
             }
           }
         }
-        // ---- O^T += V^T . P^T
+        // ---- O^T += V^T . P^T (this warp's half of D when DS = 2)
         const bool edge = r0 < lo || r0 + TW > hi;
 #pragma unroll
-        for (int dm = 0; dm < KS; ++dm) {
-          const int chunk = dm * 2 + v_chunk;
+        for (int dw = 0; dw < KSW; ++dw) {
+          const int chunk = (dh * KSW + dw) * 2 + v_chunk;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             uint32_t a[4];
@@ -318,8 +328,8 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
             }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              mma_bf16(acc[nt][dm], a, bh[mt][nt][0], bh[mt][nt][1]);
-              if (PRECISE) mma_bf16(acc[nt][dm], a, bl[mt][nt][0], bl[mt][nt][1]);
+              mma_bf16(acc[nt][dw], a, bh[mt][nt][0], bh[mt][nt][1]);
+              if (PRECISE) mma_bf16(acc[nt][dw], a, bl[mt][nt][0], bl[mt][nt][1]);
             }
           }
         }
@@ -344,20 +354,20 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float *dst = comb_acc + (cw * GC + nt * 8 + quad * 2 + j) * D + grp;
+        float *dst = comb_acc + (tg * GC + nt * 8 + quad * 2 + j) * D + dh * KSW * 16 + grp;
 #pragma unroll
-        for (int dm = 0; dm < KS; ++dm) {
+        for (int dm = 0; dm < KSW; ++dm) {
           dst[dm * 16] = acc[nt][dm][j];
           dst[dm * 16 + 8] = acc[nt][dm][j + 2];
         }
-        if (grp == 0) {
-          comb_ml[cw * 2 * GC + nt * 8 + quad * 2 + j] = m[nt][j];
-          comb_ml[cw * 2 * GC + GC + nt * 8 + quad * 2 + j] = l[nt][j];
+        if (grp == 0 && dh == 0) {
+          comb_ml[tg * 2 * GC + nt * 8 + quad * 2 + j] = m[nt][j];
+          comb_ml[tg * 2 * GC + GC + nt * 8 + quad * 2 + j] = l[nt][j];
         }
       }
     }
     named_barrier(1, NC * 32);
-    combine_and_store<D, GC, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
+    combine_and_store<D, GC, NG, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
     finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
   }
@@ -368,7 +378,7 @@ cudaError_t launch_mma_t(const KernelLaunch &L, cudaStream_t stream) {
   using S = MmaShape<D>;
   constexpr int GC = 8 * NT;
   auto kernel = mma_partition_kernel<D, NT, true>;
-  constexpr int smem = PartitionSmem<D, S::T, MmaStages<D, GC>::NS, S::NC, GC>::BYTES;
+  constexpr int smem = PartitionSmem<D, S::T, MmaStages<D, GC>::NS, S::NG, GC>::BYTES;
   static int blocks_per_sm[kMaxDevices] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);

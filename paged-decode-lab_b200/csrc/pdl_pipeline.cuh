@@ -244,15 +244,16 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
   producer_finish(p, lane);
 }
 
-// Merge NC per-warp softmax states of one item and store the outputs.
-//   comb_acc [NC][GC][D]  unnormalised accumulators (relative to each warp's max)
-//   comb_ml  [NC][2][GC]  per-warp running max (base-2 scaled units) and sum
+// Merge NC per-warp (or per-group) softmax states of one item and store the
+// outputs, with the NW consumer warps' threads (tid < NW * 32).
+//   comb_acc [NC][GC][D]  unnormalised accumulators (relative to each state's max)
+//   comb_ml  [NC][2][GC]  per-state running max (base-2 scaled units) and sum
 // M = max_w m_w; f_w = 2^(m_w - M); L = sum f_w l_w; O = sum f_w acc_w.
 // Stores O/L + LSE (natural log), (M ln2, L, O), or BF16 O/L.
-template <int D, int GC, int NC>
+template <int D, int GC, int NC, int NW = NC>
 __device__ void combine_and_store(const PartitionParams &p, const Item &w, int h0, int rows,
                                   const float *comb_acc, const float *comb_ml, int tid) {
-  for (int e = tid * 4; e < rows * D; e += NC * 32 * 4) {
+  for (int e = tid * 4; e < rows * D; e += NW * 32 * 4) {
     const int g = e / D, d = e % D;
     float mx = -INFINITY;
 #pragma unroll
