@@ -59,9 +59,9 @@ def parse_args():
     ap.add_argument("--context", type=int, default=None)
     ap.add_argument("--splits", type=int, default=None, help="matched plan split count")
     ap.add_argument("--kernel", default="auto", choices=("auto", "simt", "mma"))
-    ap.add_argument("--mode", default="batch", choices=("batch", "context"),
-                    help="N>1: independent batch per rank (weak) or one batch split by context "
-                         "across ranks (strong)")
+    ap.add_argument("--mode", default="batch", choices=("batch", "context", "head"),
+                    help="N>1: independent batch per rank (weak), one batch split by context "
+                         "across ranks (strong), or one batch split by KV head (strong)")
     ap.add_argument("--exchange", default="p2p", choices=("nccl", "p2p"),
                     help="context mode: NCCL all-gather between two merge kernels, or one "
                          "kernel storing into peers' buffers over NVLink (pdl_exchange_merge)")
@@ -403,10 +403,29 @@ def main():
         return float(t.item())
 
     context = args.mode == "context" and world > 1
-    # Context mode: every rank builds the same global batch and keeps its page range.
-    first = make_workload(args.config, device=device, batch=args.batch, context=args.context,
-                          rank=0 if context else rank)
-    kv_bytes = first.kv_bytes  # every copy has the same lengths
+    heads = args.mode == "head" and world > 1
+    strong = context or heads
+
+    def build(seed=0):
+        """This rank's workload: its own batch (batch mode), or the global batch
+        (same seed on every rank) cut to this rank's KV heads (head mode) or,
+        later, to its page range (context mode)."""
+        w = make_workload(args.config, device=device, batch=args.batch, context=args.context,
+                          rank=0 if strong else rank, seed=seed)
+        if heads:
+            from paged_decode import parallel
+            from paged_decode.spec import DecodeSpec
+            sp = w.spec
+            w.q, w.k, w.v = parallel.shard_head_pool(w.k, w.v, w.q, rank, world,
+                                                     sp.num_heads, sp.num_kv_heads)
+            w.spec = DecodeSpec(sp.max_batch, sp.num_heads // world, sp.num_kv_heads // world,
+                                sp.head_dim, sp.max_context_len)
+            torch.cuda.empty_cache()
+        return w
+
+    first = build()
+    # Job bytes: the global batch's KV bytes (strong modes) or every rank's own.
+    kv_bytes = first.kv_bytes * (world if heads else 1)
     stream = torch.cuda.current_stream(device)
     K = args.steps
     if context:
@@ -424,8 +443,10 @@ def main():
         local_bytes = int(cp.local_len.sum().item()) * first.spec.num_kv_heads * \
             first.spec.head_dim * 4
 
-        def decode_call(w):
+        def decode_call(w, slot=0):
             return cp(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale)
+
+        out_slots = None  # one output buffer: copied out per step (below)
 
         part_args = [cp._launch_args(first.q, k_loc, v_loc, t_loc, first.scale)[0]]
         out_buf = cp.out
@@ -433,18 +454,20 @@ def main():
         pool_bytes = first.k.numel() * 2 * 2
         copies = 1 if (pool_bytes >= 2 * L2_BYTES or args.hot) else \
             min(64, math.ceil(2 * L2_BYTES / pool_bytes))
-        wls = [first] + [make_workload(args.config, device=device, batch=args.batch,
-                                       context=args.context, rank=rank, seed=c)
-                         for c in range(1, copies)]
+        wls = [first] + [build(seed=c) for c in range(1, copies)]
         res = allocate_matched_resources(
             first.spec, device,
             plan=config_plan(args.config, args, first.spec, ops.sm_count(device)))
         plan = res.plan
-        local_bytes = kv_bytes
+        local_bytes = first.kv_bytes
 
-        def decode_call(w):
-            return matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res,
-                                  scale=w.scale, kernel=args.kernel)
+        # A second resource set lets step i+1 compute while step i's output
+        # is still being copied to the host.
+        out_slots = [res, allocate_matched_resources(first.spec, device, plan=plan)]
+
+        def decode_call(w, slot=0):
+            return matched_decode(w.q, w.k, w.v, w.table, w.lengths,
+                                  resources=out_slots[slot], scale=w.scale, kernel=args.kernel)
 
         part_args = [ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
                                      tokens_per_split=plan.tokens_per_split, splits=plan.splits,
@@ -502,7 +525,7 @@ def main():
     step_graph = capture(step)
     total_ms, reps = timed(step_graph, args.window_seconds)
     ms_per_step = total_ms / (reps * K)
-    job_bytes = kv_bytes if context else world * kv_bytes
+    job_bytes = kv_bytes if strong else world * kv_bytes
     value = job_bytes / (ms_per_step / 1e3) / 1e9
 
     part_graph = capture(partition_only)
@@ -519,6 +542,10 @@ def main():
     # lengths) sit in one pinned staging buffer, copied to the device with one
     # H2D copy (the workload tensors are views into its device twin, as a
     # serving engine stages them); the output is copied back to pinned memory.
+    # As in a serving loop, copies run on their own streams, double-buffered:
+    # step i+1's inputs are copied in and step i's output is copied out while
+    # the next step computes.  Every copy of every step is inside the timed
+    # region (the end event waits for the last copy out).
     def staged(w):
         parts = [w.q, w.table, w.lengths]
         sizes = [t.numel() * t.element_size() for t in parts]
@@ -535,15 +562,43 @@ def main():
         host.copy_(dev)
         return dev, host
 
-    stages = [staged(w) for w in wls]
-    hout = torch.empty(out_buf.shape, dtype=out_buf.dtype).pin_memory()
+    e2e_wls = list(wls)
+    if len(e2e_wls) < 2:  # a second staging set for the same workload
+        import copy as _copy
+        twin = _copy.copy(first)
+        twin.q, twin.table, twin.lengths = (first.q.clone(), first.table.clone(),
+                                            first.lengths.clone())
+        e2e_wls.append(twin)
+    stages = [staged(w) for w in e2e_wls]
+    n_stage = len(stages)
+    hout = [torch.empty(out_buf.shape, dtype=out_buf.dtype).pin_memory() for _ in range(2)]
+    dout = None if out_slots is not None else [torch.empty_like(out_buf) for _ in range(2)]
     h2d = stages[0][0].numel()
-    d2h = hout.numel() * hout.element_size()
+    d2h = hout[0].numel() * hout[0].element_size()
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready, stage_free = [ev() for _ in range(n_stage)], [ev() for _ in range(n_stage)]
+    computed, out_free = [ev(), ev()], [ev(), ev()]
 
     def e2e_step(i):
-        dev, host = stages[i % copies]
-        dev.copy_(host, non_blocking=True)
-        hout.copy_(decode_call(wls[i % copies]), non_blocking=True)
+        s, j = i % n_stage, i % 2
+        dev, host = stages[s]
+        copy_in.wait_event(stage_free[s])           # step i - n_stage has read it
+        with torch.cuda.stream(copy_in):
+            dev.copy_(host, non_blocking=True)
+        in_ready[s].record(copy_in)
+        stream.wait_event(in_ready[s])
+        stream.wait_event(out_free[j])               # step i - 2's output is on the host
+        out = decode_call(e2e_wls[s], j)
+        if dout is not None:
+            dout[j].copy_(out, non_blocking=True)
+            out = dout[j]
+        stage_free[s].record(stream)
+        computed[j].record(stream)
+        copy_out.wait_event(computed[j])
+        with torch.cuda.stream(copy_out):
+            hout[j].copy_(out, non_blocking=True)
+        out_free[j].record(copy_out)
 
     for i in range(3):
         e2e_step(i)
@@ -552,8 +607,10 @@ def main():
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    copy_in.wait_stream(stream)  # the first copy in starts after the start event
     for i in range(K):
         e2e_step(i)
+    stream.wait_stream(copy_out)
     e1.record(stream)
     torch.cuda.synchronize(device)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -566,12 +623,12 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
             "us_per_call": round(ms_per_step * 1e3, 3), "higher_is_better": True,
-            "scaling": "strong" if context else "weak", "vs_baseline": None,
+            "scaling": "strong" if strong else "weak", "vs_baseline": None,
             "dtype": "bf16 in, fp32 softmax/accumulate",
             "data": "synthetic (seeded N(0,1) BF16 q/K/V, shuffled page pool)",
             "config": {"workload": args.config, "batch": first.spec.max_batch,
-                       "num_heads": first.spec.num_heads,
-                       "num_kv_heads": first.spec.num_kv_heads,
+                       "num_heads": first.spec.num_heads * (world if heads else 1),
+                       "num_kv_heads": first.spec.num_kv_heads * (world if heads else 1),
                        "head_dim": first.spec.head_dim, "context": first.spec.max_context_len,
                        "splits": plan.splits, "tokens_per_split": plan.tokens_per_split,
                        "kv_bytes_per_step": kv_bytes, "kernel": kernel_name,
@@ -579,7 +636,8 @@ def main():
                                        + ("one peer-memory exchange kernel over NVLink"
                                           if args.exchange == "p2p" else
                                           "NCCL all-gather + LSE merge") + ")"
-                                       if context else f"batch-sharded x{world}" if world > 1
+                                       if context else f"KV-head-sharded x{world}" if heads
+                                       else f"batch-sharded x{world}" if world > 1
                                        else "single GPU"),
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",
                        "l2": ("inputs larger than L2 (KV pool >> 126 MB)"

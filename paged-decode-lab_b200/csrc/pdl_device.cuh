@@ -167,6 +167,27 @@ __device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Host: launch `kernel` with programmatic stream serialization, so it may be
+// scheduled while the previous kernel in the stream still runs (once that
+// kernel has executed allow_dependent_launch in every CTA); the kernel must
+// call grid_dependency_wait before touching anything the previous kernels
+// write or read.  Without such a trigger it behaves like a plain launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_programmatic(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 constexpr float LN2 = 0.6931471805599453f;
 
 }  // namespace pdl

@@ -92,8 +92,11 @@ __global__ void __launch_bounds__(32 * kExchangeWarps, kExchangeCtasPerSm)
   __nv_bfloat16 *out = p.out + rank_slice * p.rows * D;
   uint32_t *own_seq = reinterpret_cast<uint32_t *>(p.buffers[rank]);
 
-  // The local partitions are the previous kernel's output, and this rank's
-  // previous exchange may still read the buffers until it completes.
+  // The next step's partition kernel may be scheduled now (it waits for this
+  // grid before touching anything).  The local partitions are the previous
+  // kernel's output, and this rank's previous exchange may still read the
+  // buffers until it completes.
+  allow_dependent_launch();
   grid_dependency_wait();
   const uint32_t seq = __shfl_sync(FULL_MASK, lane == 0 ? own_seq[warp] + 1u : 0u, 0);
   const int64_t half = (int64_t)(seq & 1u) * p.world * p.block;

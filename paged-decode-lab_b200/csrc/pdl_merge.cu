@@ -35,6 +35,9 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   const int lane = threadIdx.x & 31;
   const int unit = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
   const int row = unit / SLICES, col0 = (unit % SLICES) * CW;
+  // The next decode step's partition kernel may be scheduled now; it waits
+  // for this grid to complete before touching the workspace.
+  allow_dependent_launch();
   // Lengths are an input of the decode, not an output of the partition
   // kernel, so they are read before waiting for it.
   int live = p.splits;
@@ -69,17 +72,8 @@ cudaError_t launch_merge_t(const MergeParams &params, cudaStream_t stream) {
   const int64_t units = (int64_t)params.rows * SLICES;
   const int grid = (int)((units + MERGE_WARPS - 1) / MERGE_WARPS);
   if (grid <= 0) return cudaSuccess;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(32 * MERGE_WARPS);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_kernel<D>, params);
+  return launch_programmatic(merge_kernel<D>, dim3(grid), dim3(32 * MERGE_WARPS), 0, stream,
+                             params);
 }
 
 }  // namespace

@@ -140,6 +140,11 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     mbar_init_fence();
   }
   __syncthreads();
+  // Launched with programmatic stream serialization: the set-up above may
+  // overlap the previous kernel; its outputs (q, lengths, block table, the
+  // workspace and scheduler words it may still read) are touched only after
+  // it has completed.
+  grid_dependency_wait();
 
   if (warp == 0) {
     run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, ring, lane);
@@ -394,8 +399,8 @@ cudaError_t launch_mma_t(const KernelLaunch &L, cudaStream_t stream) {
   }
   const int grid = min(L.params.n_items, blocks_per_sm[dev] * L.sm_count);
   if (grid <= 0) return cudaSuccess;
-  kernel<<<grid, S::NTHREADS, smem, stream>>>(*L.k_map, *L.v_map, L.params);
-  return cudaGetLastError();
+  return launch_programmatic(kernel, dim3(grid), dim3(S::NTHREADS), smem, stream, *L.k_map,
+                             *L.v_map, L.params);
 }
 
 template <int D>
