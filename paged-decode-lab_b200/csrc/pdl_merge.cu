@@ -1,9 +1,11 @@
 // pdl_merge.cu -- stable merge of split-K partitions.
 //
 // One warp per (row, query head, column slice of at most 128 floats); lane l
-// owns 4 (or D/32 for D = 64) contiguous FP32 columns of the slice, so each
-// partition row is read with one coalesced vector load per lane, and rows of
-// eight partitions are in flight at once.  The kernel is launched with
+// owns 4 (or D/32 for D = 64) contiguous FP32 columns of the slice.  The
+// rows of up to min(splits, 32) partitions are copied into shared memory
+// asynchronously (one 16- or 8-byte cp.async per lane and partition) while
+// the weights are loaded and reduced, so a merge costs about one memory
+// round trip.  The kernel is launched with
 // programmatic stream serialization: its CTAs may be scheduled while the
 // partition kernel still runs and wait (griddepcontrol.wait) for it to
 // complete before reading anything.
@@ -51,9 +53,12 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
   const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;
   const float *l_src = lse_protocol ? nullptr : p.denoms + (int64_t)row * p.w_row_stride;
+  extern __shared__ __align__(16) float merge_stage[];
+  const int cap = min(p.splits, 32);
   float acc[E], shift, tot;
-  merge_slice<E, (E <= 4 ? 16 : 8), false>(lse_protocol, w_src, p.w_part_stride, l_src, r_src,
-                                          p.part_stride, live, lane, acc, shift, tot);
+  merge_slice_staged<E>(lse_protocol, w_src, p.w_part_stride, l_src, r_src, p.part_stride, live,
+                        lane, merge_stage + (threadIdx.x >> 5) * cap * 32 * E, cap, acc, shift,
+                        tot);
   if (p.out != nullptr) {
     __nv_bfloat16 *dst = p.out + (int64_t)row * D + col0 + lane * E;
 #pragma unroll
@@ -68,11 +73,26 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
 
 template <int D>
 cudaError_t launch_merge_t(const MergeParams &params, cudaStream_t stream) {
-  constexpr int SLICES = D / (D < 128 ? D : 128);
+  constexpr int CW = D < 128 ? D : 128;
+  constexpr int SLICES = D / CW;
+  // Up to 32 staged partition rows of CW floats per warp.
+  constexpr int max_smem = MERGE_WARPS * 32 * CW * 4;
+  const int smem = MERGE_WARPS * (params.splits < 32 ? params.splits : 32) * CW * 4;
+  static bool configured[kMaxDevices] = {false};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    err = cudaFuncSetAttribute(merge_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               max_smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = true;
+  }
   const int64_t units = (int64_t)params.rows * SLICES;
   const int grid = (int)((units + MERGE_WARPS - 1) / MERGE_WARPS);
   if (grid <= 0) return cudaSuccess;
-  return launch_programmatic(merge_kernel<D>, dim3(grid), dim3(32 * MERGE_WARPS), 0, stream,
+  return launch_programmatic(merge_kernel<D>, dim3(grid), dim3(32 * MERGE_WARPS), smem, stream,
                              params);
 }
 

@@ -133,4 +133,99 @@ __device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_sr
   for (int e = 0; e < E; ++e) acc[e] *= scale;
 }
 
+// ---------------------------------------------------------------------------
+// merge_slice with the partition rows staged through shared memory: every
+// lane issues one asynchronous copy per partition (cp.async, L2 only) for up
+// to `cap` partitions before the weights are reduced, so the rows arrive in one
+// round trip that overlaps the weights' instead of one per BATCH partitions.
+// The arithmetic and its order are those of merge_slice, so the bits are too.
+// `stage` is this warp's cap * 32 * E floats of shared memory.
+template <int E>
+__device__ __forceinline__ void stage_rows(float *stage, const float *r_src, int64_t part_stride,
+                                           int first, int n, int lane) {
+  const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(stage + lane * E));
+  for (int j = 0; j < n; ++j) {
+    const float *src = r_src + (int64_t)(first + j) * part_stride + lane * E;
+    const uint32_t dst = dst0 + j * 32 * E * 4;
+    if constexpr (E == 4) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    } else {
+      static_assert(E == 2, "two or four columns per lane");
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void wait_staged_rows() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncwarp();
+}
+
+// Rows are staged `cap` (<= 32) partitions at a time.
+template <int E>
+__device__ __forceinline__ void merge_slice_staged(bool lse_protocol, const float *w_src,
+                                                   int64_t w_part_stride, const float *l_src,
+                                                   const float *r_src, int64_t part_stride,
+                                                   int live, int lane, float *stage, int cap,
+                                                   float (&acc)[E], float &shift, float &tot) {
+  stage_rows<E>(stage, r_src, part_stride, 0, min(live, cap), lane);
+  constexpr int WR = 4;
+  float wreg[WR];
+#pragma unroll
+  for (int i = 0; i < WR; ++i)
+    wreg[i] = lane + 32 * i < live ? __ldcg(w_src + (lane + 32 * i) * w_part_stride) : -INFINITY;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < WR; ++i) mx = fmaxf(mx, wreg[i]);
+  for (int s = lane + 32 * WR; s < live; s += 32) mx = fmaxf(mx, __ldcg(w_src + s * w_part_stride));
+  mx = warp_max_all(mx);
+  if (mx == -INFINITY) mx = 0.f;
+
+  shift = mx;
+  float scale = 1.f;
+  tot = 0.f;
+  if (lse_protocol) {
+#pragma unroll
+    for (int i = 0; i < WR; ++i) tot += lane + 32 * i < live ? expf(wreg[i] - mx) : 0.f;
+    for (int s = lane + 32 * WR; s < live; s += 32) tot += expf(__ldcg(w_src + s * w_part_stride) - mx);
+    tot = warp_sum_all(tot);
+    shift = tot > 0.f ? logf(tot) + mx : INFINITY;
+  } else {
+    for (int s = lane; s < live; s += 32)
+      tot += __ldcg(l_src + s * w_part_stride) * expf(__ldcg(w_src + s * w_part_stride) - mx);
+    tot = warp_sum_all(tot);
+    scale = 1.f / (tot > 0.f ? tot : 1.f);
+  }
+
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  for (int s0 = 0; s0 < live; s0 += 32) {
+    const int n = min(32, live - s0);
+    const int wi = s0 / 32;
+    // Register select (a dynamic index would put wreg in local memory).
+    const float wsrc = wi == 0 ? wreg[0] : wi == 1 ? wreg[1] : wi == 2 ? wreg[2]
+                     : wi == 3 ? wreg[3]
+                     : (s0 + lane < live ? __ldcg(w_src + (s0 + lane) * w_part_stride)
+                                         : -INFINITY);
+    const float wl = (s0 + lane < live) ? expf(wsrc - shift) : 0.f;
+    for (int c0 = 0; c0 < n; c0 += cap) {
+      const int m = min(cap, n - c0);
+      if (s0 + c0 > 0) {
+        __syncwarp();  // every lane is done with the previous rows
+        stage_rows<E>(stage, r_src, part_stride, s0 + c0, m, lane);
+      }
+      wait_staged_rows();
+      for (int j = 0; j < m; ++j) {
+        const float wk = __shfl_sync(FULL_MASK, wl, c0 + j);
+        const float *row = stage + j * 32 * E + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, row[e], acc[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] *= scale;
+}
+
 }  // namespace pdl
