@@ -65,6 +65,10 @@ def parse_args():
     ap.add_argument("--exchange", default="p2p", choices=("nccl", "p2p"),
                     help="context mode: NCCL all-gather between two merge kernels, or one "
                          "kernel storing into peers' buffers over NVLink (pdl_exchange_merge)")
+    ap.add_argument("--append", action="store_true",
+                    help="each step first appends the new token's K/V through the block table "
+                         "(pdl_append_kv, lengths += 1 on the device) and then decodes, as a "
+                         "decode loop does; lengths restart at each replayed window")
     ap.add_argument("--hot", action="store_true",
                     help="reuse one input copy every step (L2-resident when it fits), as the "
                          "reference measured its A100 numbers; default rotates copies past L2")
@@ -404,6 +408,8 @@ def main():
 
     context = args.mode == "context" and world > 1
     heads = args.mode == "head" and world > 1
+    if args.append and context:
+        raise SystemExit("--append is not supported with --mode context")
     strong = context or heads
 
     def build(seed=0):
@@ -465,7 +471,18 @@ def main():
         # is still being copied to the host.
         out_slots = [res, allocate_matched_resources(first.spec, device, plan=plan)]
 
+        if args.append:
+            from paged_decode.kvcache import append_decode_kv
+            for w in wls:
+                gen = torch.Generator(device=device).manual_seed(99)
+                shape = (w.spec.max_batch, w.spec.num_kv_heads, w.spec.head_dim)
+                w.k_new = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+                w.v_new = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+                w.len0 = w.lengths.clone()
+
         def decode_call(w, slot=0):
+            if args.append:
+                append_decode_kv(w.k_new, w.v_new, w.k, w.v, w.table, w.lengths)
             return matched_decode(w.q, w.k, w.v, w.table, w.lengths,
                                   resources=out_slots[slot], scale=w.scale, kernel=args.kernel)
 
@@ -477,6 +494,8 @@ def main():
         out_buf = res.out
 
     def step(i):
+        if args.append and i < copies:  # each window starts from the same lengths
+            wls[i].lengths.copy_(wls[i].len0)
         decode_call(wls[i % copies])
 
     def partition_only(i):
@@ -640,6 +659,8 @@ def main():
                                        else f"batch-sharded x{world}" if world > 1
                                        else "single GPU"),
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",
+                       "step": ("KV append (lengths += 1 on the device) + decode; KV bytes "
+                                "counted at the starting lengths" if args.append else "decode"),
                        "l2": ("inputs larger than L2 (KV pool >> 126 MB)"
                               if copies == 1 and not args.hot else
                               "hot: one input copy reused every step (L2-resident)" if args.hot
@@ -655,7 +676,8 @@ def main():
                             else "paged_decode.matched_splitkv.matched_decode")},
             # Own kernels per step: partition + merge; context mode adds the
             # local merge (nccl) or replaces both merges by the exchange (p2p).
-            "gpu_launches": ((3 if args.exchange == "nccl" else 2) if context else 2) * K * reps,
+            "gpu_launches": (((3 if args.exchange == "nccl" else 2) if context else 2)
+                             + (1 if args.append else 0)) * K * reps,
             "clocks": clocks.summary(windows),
             "fault_word": fault,
         }

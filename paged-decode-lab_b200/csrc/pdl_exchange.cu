@@ -6,8 +6,9 @@
 // Each warp owns a fixed list of units (row, column slice), the same list on
 // every rank, and for each of them:
 //
-//   1. merges this rank's partitions and stores the merged FP32 partial and
-//      LSE into block `rank` of EVERY rank's exchange buffer (peer stores
+//   1. merges this rank's partitions (rows staged through shared memory with
+//      cp.async, as in the merge kernel) and stores the merged FP32 partial
+//      and LSE into block `rank` of EVERY rank's exchange buffer (peer stores
 //      over NVLink), each float as one 8-byte word (float bits | sequence
 //      << 32) written with a single-copy-atomic relaxed system-scope store;
 //   2. reads the `world` blocks of the unit from this GPU's own buffer,
@@ -68,6 +69,15 @@ __device__ __forceinline__ uint64_t load_word(const uint64_t *p) {
   return a;
 }
 
+constexpr int kExchangeStageParts = 16;
+
+// Shared memory of one exchange CTA: each warp stages up to 16 partition
+// rows of its column slice (at most 32 KB, so kExchangeCtasPerSm CTAs fit).
+constexpr size_t exchange_smem_bytes(int head_dim, int splits) {
+  return (size_t)kExchangeWarps * (splits < kExchangeStageParts ? splits : kExchangeStageParts) *
+         (head_dim < 128 ? head_dim : 128) * 4;
+}
+
 __device__ __forceinline__ uint64_t *block_of(unsigned char *buffer, int64_t half, int rank,
                                               int64_t block) {
   return reinterpret_cast<uint64_t *>(buffer + kExchangeHeaderBytes) + half + rank * block;
@@ -91,6 +101,10 @@ __global__ void __launch_bounds__(32 * kExchangeWarps, kExchangeCtasPerSm)
       p.lengths != nullptr ? p.lengths + rank_slice * (p.rows / p.num_heads) : nullptr;
   __nv_bfloat16 *out = p.out + rank_slice * p.rows * D;
   uint32_t *own_seq = reinterpret_cast<uint32_t *>(p.buffers[rank]);
+  // Local partition rows are staged through shared memory, up to
+  // kExchangeStageParts at a time per warp.
+  extern __shared__ __align__(16) float stage[];
+  const int stage_cap = min(p.splits, kExchangeStageParts);
 
   // The next step's partition kernel may be scheduled now (it waits for this
   // grid before touching anything).  The local partitions are the previous
@@ -110,9 +124,10 @@ __global__ void __launch_bounds__(32 * kExchangeWarps, kExchangeCtasPerSm)
       live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
     }
     float acc[E], shift, tot;
-    merge_slice<E, 8, false>(true, lse + (int64_t)row * p.splits, 1, nullptr,
-                             partial + (int64_t)row * p.splits * D + col0, D, live, lane, acc,
-                             shift, tot);
+    merge_slice_staged<E>(true, lse + (int64_t)row * p.splits, 1, nullptr,
+                          partial + (int64_t)row * p.splits * D + col0, D, live, lane,
+                          stage + (threadIdx.x >> 5) * stage_cap * 32 * E, stage_cap, acc, shift,
+                          tot);
     const uint64_t lse_word = pack_word(tot > 0.f ? shift : -INFINITY, seq);
     for (int q = 0; q < p.world; ++q) {
       uint64_t *dst = block_of(p.buffers[q], half, rank, p.block);
@@ -198,7 +213,7 @@ cudaError_t launch_exchange_t(const ExchangeParams &params, cudaStream_t stream)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(params.ctas, params.emulate ? params.world : 1);
   cfg.blockDim = dim3(32 * kExchangeWarps);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = exchange_smem_bytes(D, params.splits);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   if (params.emulate) {
