@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(32 * kExchangeWarps, kExchangeCtasPerSm)
       live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
     }
     float acc[E], shift, tot;
-    merge_slice_staged<E>(true, lse + (int64_t)row * p.splits, 1, nullptr,
+    merge_slice<E>(true, lse + (int64_t)row * p.splits, 1, nullptr,
                           partial + (int64_t)row * p.splits * D + col0, D, live, lane,
                           stage + (threadIdx.x >> 5) * stage_cap * 32 * E, stage_cap, acc, shift,
                           tot);

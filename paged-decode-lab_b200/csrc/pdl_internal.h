@@ -18,7 +18,8 @@ enum OutMode : int {
 };
 
 // Work item = (row b, KV head, head sub-group, partition); items are
-// enumerated partition-fastest and handed to persistent CTAs round-robin.
+// enumerated partition-fastest and handed to persistent CTAs round-robin, or
+// partition-major from an atomic counter (dynamic scheduling, `sched`).
 struct PartitionParams {
   const __nv_bfloat16 *q;
   int64_t q_stride_batch;   // elements

@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   extern __shared__ __align__(16) float merge_stage[];
   const int cap = min(p.splits, 32);
   float acc[E], shift, tot;
-  merge_slice_staged<E>(lse_protocol, w_src, p.w_part_stride, l_src, r_src, p.part_stride, live,
+  merge_slice<E>(lse_protocol, w_src, p.w_part_stride, l_src, r_src, p.part_stride, live,
                         lane, merge_stage + (threadIdx.x >> 5) * cap * 32 * E, cap, acc, shift,
                         tot);
   if (p.out != nullptr) {

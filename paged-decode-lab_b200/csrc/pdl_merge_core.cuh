@@ -13,28 +13,14 @@
 //   M = max_p m_p (-inf -> 0); f_p = exp(m_p - M);
 //   out = sum_p f_p * acc_p / (sum_p f_p * l_p, or 1 when that is 0).
 // Partitions are accumulated in index order with one fused multiply-add per
-// partition, whatever the batching of the loads.
+// partition, whatever the staging of the loads; the fused merge of the
+// partition kernels (merge_group) and the exchange kernel's merge across
+// ranks keep the same order, so all of them give the same bits.
 #pragma once
 
 #include "pdl_device.cuh"
 
 namespace pdl {
-
-template <int E, bool CG>
-__device__ __forceinline__ void merge_load_cols(const float *src, float (&v)[E]) {
-  if constexpr (E == 2) {
-    const float2 a = CG ? __ldcg(reinterpret_cast<const float2 *>(src))
-                        : *reinterpret_cast<const float2 *>(src);
-    v[0] = a.x; v[1] = a.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < E; i += 4) {
-      const float4 a = CG ? __ldcg(reinterpret_cast<const float4 *>(src + i))
-                          : *reinterpret_cast<const float4 *>(src + i);
-      v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
-    }
-  }
-}
 
 template <int E>
 __device__ __forceinline__ void merge_store_cols(float *dst, const float (&v)[E]) {
@@ -59,87 +45,12 @@ __device__ __forceinline__ float warp_sum_all(float v) {
   return v;
 }
 
-// Merges `live` partitions into acc (already scaled).  `shift` is the
-// exponent subtracted from every weight (the LSE protocol's logsum), `tot`
-// the weight total, so the merged LSE is (tot > 0 ? shift : -inf).
-// CG: read partition rows through L2 only (rows written by other GPUs
-// during the kernel must not be served from a stale L1 line).
-template <int E, int BATCH, bool CG>
-__device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_src,
-                                            int64_t w_part_stride, const float *l_src,
-                                            const float *r_src, int64_t part_stride, int live,
-                                            int lane, float (&acc)[E], float &shift,
-                                            float &tot) {
-  // Weights of partitions lane, lane+32, ... stay in registers (up to 128
-  // partitions; more are re-read).
-  constexpr int WR = 4;
-  float wreg[WR];
-#pragma unroll
-  for (int i = 0; i < WR; ++i)
-    wreg[i] = lane + 32 * i < live ? __ldcg(w_src + (lane + 32 * i) * w_part_stride) : -INFINITY;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < WR; ++i) mx = fmaxf(mx, wreg[i]);
-  for (int s = lane + 32 * WR; s < live; s += 32) mx = fmaxf(mx, __ldcg(w_src + s * w_part_stride));
-  mx = warp_max_all(mx);
-  if (mx == -INFINITY) mx = 0.f;
-
-  shift = mx;
-  float scale = 1.f;
-  tot = 0.f;
-  if (lse_protocol) {
-#pragma unroll
-    for (int i = 0; i < WR; ++i) tot += lane + 32 * i < live ? expf(wreg[i] - mx) : 0.f;
-    for (int s = lane + 32 * WR; s < live; s += 32) tot += expf(__ldcg(w_src + s * w_part_stride) - mx);
-    tot = warp_sum_all(tot);
-    shift = tot > 0.f ? logf(tot) + mx : INFINITY;
-  } else {
-    for (int s = lane; s < live; s += 32)
-      tot += __ldcg(l_src + s * w_part_stride) * expf(__ldcg(w_src + s * w_part_stride) - mx);
-    tot = warp_sum_all(tot);
-    scale = 1.f / (tot > 0.f ? tot : 1.f);
-  }
-
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int s0 = 0; s0 < live; s0 += 32) {
-    const int wi = s0 / 32;
-    // Register select (a dynamic index would put wreg in local memory).
-    const float wsrc = wi == 0 ? wreg[0] : wi == 1 ? wreg[1] : wi == 2 ? wreg[2]
-                     : wi == 3 ? wreg[3]
-                     : (s0 + lane < live ? __ldcg(w_src + (s0 + lane) * w_part_stride)
-                                         : -INFINITY);
-    const float wl = (s0 + lane < live) ? expf(wsrc - shift) : 0.f;
-    const int n = min(32, live - s0);
-    // Rows of up to BATCH partitions are loaded before any is consumed, so
-    // the memory round trips overlap instead of serialising per partition.
-    for (int k0 = 0; k0 < n; k0 += BATCH) {
-      float v[BATCH][E];
-#pragma unroll
-      for (int j = 0; j < BATCH; ++j)
-        merge_load_cols<E, CG>(r_src + (int64_t)(s0 + min(k0 + j, n - 1)) * part_stride + lane * E,
-                               v[j]);
-#pragma unroll
-      for (int j = 0; j < BATCH; ++j) {
-        const float wk = __shfl_sync(FULL_MASK, wl, min(k0 + j, 31));
-        if (k0 + j < n) {
-#pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, v[j][e], acc[e]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] *= scale;
-}
-
 // ---------------------------------------------------------------------------
-// merge_slice with the partition rows staged through shared memory: every
-// lane issues one asynchronous copy per partition (cp.async, L2 only) for up
-// to `cap` partitions before the weights are reduced, so the rows arrive in one
-// round trip that overlaps the weights' instead of one per BATCH partitions.
-// The arithmetic and its order are those of merge_slice, so the bits are too.
-// `stage` is this warp's cap * 32 * E floats of shared memory.
+// The partition rows are staged through shared memory: every lane issues one
+// asynchronous copy (cp.async, L2 only) per partition for up to `cap`
+// partitions before the weights are even reduced, so the rows arrive in one
+// round trip that overlaps the weights'.  `stage` is this warp's
+// cap * 32 * E floats of shared memory.
 template <int E>
 __device__ __forceinline__ void stage_rows(float *stage, const float *r_src, int64_t part_stride,
                                            int first, int n, int lane) {
@@ -162,9 +73,12 @@ __device__ __forceinline__ void wait_staged_rows() {
   __syncwarp();
 }
 
-// Rows are staged `cap` (<= 32) partitions at a time.
+// Merges `live` partitions into acc (already scaled).  `shift` is the
+// exponent subtracted from every weight (the LSE protocol's logsum), `tot`
+// the weight total, so the merged LSE is (tot > 0 ? shift : -inf).  Rows are
+// staged `cap` (<= 32) partitions at a time.
 template <int E>
-__device__ __forceinline__ void merge_slice_staged(bool lse_protocol, const float *w_src,
+__device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_src,
                                                    int64_t w_part_stride, const float *l_src,
                                                    const float *r_src, int64_t part_stride,
                                                    int live, int lane, float *stage, int cap,
