@@ -212,3 +212,19 @@ def test_qwen35_slot_paged_update_and_matched_decode():
         assert_out_close(out, expected(q, k, v, tables, lengths, 0.0625), what=f"graph p={p}")
     del graph
     assert np.isfinite(out.float().cpu().numpy()).all()
+
+
+@pytest.mark.filterwarnings("ignore:The CUDA Graph is empty")
+def test_metadata_validation_refuses_to_run_inside_a_capture():
+    """The debug check synchronises, so during stream capture it raises
+    RuntimeError instead (reference runtime.py:38-43)."""
+    from paged_decode.runtime import validate_device_metadata
+    table = torch.zeros(1, 4, dtype=torch.int32, device=DEV)
+    lens = torch.ones(1, dtype=torch.int32, device=DEV)
+    validate_device_metadata(table, lens, 1, 1024)  # eager: fine
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(DEV)
+    with pytest.raises(RuntimeError, match="capture"):
+        with torch.cuda.graph(graph, stream=side):
+            validate_device_metadata(table, lens, 1, 1024)
+    del graph
