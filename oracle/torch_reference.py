@@ -39,3 +39,37 @@ def dense_lse(q, k, v, tables, lengths, start, stop, scale=None):
         scores = torch.einsum("hd,nhd->hn", q[b].float(), keys) * scale
         lse[b] = torch.logsumexp(scores, dim=-1)
     return lse
+
+
+def chunked_reference_rows(q, k, v, tables, lengths, rows, scale=None, chunk=65536):
+    """FP64 decode output [len(rows), Hq, D] of the selected rows, for rows too long
+    to gather whole (a 524,288-token row): per KV head, tokens in chunks, with a
+    running max / sum / weighted sum in FP64 -- the same dense softmax, only
+    evaluated piecewise.  Rows of length 0 give zeros."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    hkv = k.shape[2]
+    group = q.shape[1] // hkv
+    out = torch.zeros((len(rows), q.shape[1], q.shape[2]), dtype=torch.float64, device=q.device)
+    lens = lengths.cpu().tolist()
+    for i, b in enumerate(rows):
+        n = lens[b]
+        for h in range(hkv):
+            qh = q[b, h * group:(h + 1) * group].double()             # [G, D]
+            m = torch.full((group, 1), float("-inf"), dtype=torch.float64, device=q.device)
+            s = torch.zeros((group, 1), dtype=torch.float64, device=q.device)
+            acc = torch.zeros((group, q.shape[2]), dtype=torch.float64, device=q.device)
+            for t0 in range(0, n, chunk):
+                t = torch.arange(t0, min(n, t0 + chunk), device=q.device)
+                pages = tables[b, t // 256].long()
+                keys = k[pages, t % 256, h].double()                   # [n, D]
+                vals = v[pages, t % 256, h].double()
+                sc = (qh @ keys.T) * scale                              # [G, n]
+                m_new = torch.maximum(m, sc.max(dim=1, keepdim=True).values)
+                alpha = torch.exp(m - m_new)
+                p = torch.exp(sc - m_new)
+                s = s * alpha + p.sum(dim=1, keepdim=True)
+                acc = acc * alpha + p @ vals
+                m = m_new
+            if n:
+                out[i, h * group:(h + 1) * group] = acc / s
+    return out
