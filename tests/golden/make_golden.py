@@ -17,6 +17,7 @@ The fixtures store outputs and input checksums only; inputs are rebuilt from
 their seeds by ``cases.py``.  Nothing at test time reads the reference.
 """
 import argparse
+import os
 import importlib
 import json
 import sys
@@ -83,8 +84,12 @@ def record_case(out, meta, name, case, ref, parts=(512, 1024), scale_mul=None):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-src", default="/root/reference/src")
+    parser.add_argument("--reference-src", default=os.environ.get("PAGED_DECODE_REFERENCE_SRC"),
+                        help="the reference project's src/ directory (or set "
+                             "PAGED_DECODE_REFERENCE_SRC)")
     args = parser.parse_args()
+    if not args.reference_src:
+        parser.error("--reference-src is required")
     ref, spec_mod, plan_mod = load_reference(args.reference_src)
 
     out, meta = {}, {}
