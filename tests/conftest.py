@@ -15,3 +15,14 @@ for path in (ROOT, ROOT / "paged-decode-lab_b200", ROOT / "tests" / "golden"):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def pytest_sessionstart(session):
+    """Build the sm_100a library once if this checkout has none yet (nvcc
+    cross-compiles without a GPU); an existing build is left as it is."""
+    library = ROOT / "paged-decode-lab_b200" / "paged_decode" / "libpdl_b200.so"
+    if not library.exists():
+        csrc = ROOT / "paged-decode-lab_b200" / "csrc"
+        sys.path.insert(0, str(csrc))
+        import importlib
+        importlib.import_module("build").build()
