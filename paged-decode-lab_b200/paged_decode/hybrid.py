@@ -2,10 +2,13 @@
 
 The reference's runner (``src/paged_decode/hybrid.py``) keeps its
 full-attention layers' KV in a paged pool and calls this operator for decode.
-These are the three places where it touches the operator, with the same
+These are the places where it touches the operator, with the same
 names, arguments and errors; the model, its Transformers blocks and the
 linear-attention state are not part of this package:
 
+* ``HYBRID_BACKENDS`` / ``validate_hybrid_options`` -- the runner's option
+  check (reference ``hybrid_options.py:1-19``): the engine backends plus the
+  fixed-geometry ``triton_matched``;
 * ``allocate_hybrid_resources`` -- reference ``hybrid.py:15-21``;
 * ``paged_update`` -- the paged write of ``PagedHybridCache.update``
   (``hybrid.py:63-72``): the chunk's K/V rows go to
@@ -20,7 +23,26 @@ import torch
 
 from .kvcache import store_kvcache
 from .runtime import allocate_resources, paged_decode
-from .spec import PAGE_SIZE
+from .spec import BACKENDS, PAGE_SIZE
+
+# The engine's scheduler may change batch and table geometry between steps,
+# so its backend list leaves out the capacity-aligned fixed-plan path, which
+# only the fixed-batch runner offers.
+HYBRID_BACKENDS = (*BACKENDS, "triton_matched")
+
+
+def validate_hybrid_options(backend, mode, batch, max_context):
+    """Reject runner options before anything is loaded (same messages as the reference)."""
+    if backend not in HYBRID_BACKENDS:
+        raise ValueError(f"unknown Qwen3.5 backend {backend!r}; choose {HYBRID_BACKENDS}")
+    if mode not in ("eager", "graph"):
+        raise ValueError("execution mode must be eager or graph")
+    if type(batch) is not int or batch < 1:
+        raise ValueError("batch must be a positive integer")
+    if type(max_context) is not int or max_context < 1:
+        raise ValueError("max_context must be a positive integer")
+    if mode == "graph" and max_context < 3:
+        raise ValueError("Graph warmup needs context capacity >=3")
 
 
 def allocate_hybrid_resources(spec, device, backend):

@@ -5,17 +5,20 @@
 resource set, ``flash_attn`` leaves the model alone, non-BF16 caches and
 models without attention layers are rejected.  ``allocate_hybrid_resources``
 and ``decode_attention`` follow the Qwen3.5 runner's slot
-(src/paged_decode/hybrid.py:15-21, 80-95).
+(src/paged_decode/hybrid.py:15-21, 80-95), ``validate_hybrid_options`` its
+option check (src/paged_decode/hybrid_options.py:1-19, tests
+tests/test_hybrid_options.py:8-25).
 """
 from types import SimpleNamespace
 
 import pytest
 import torch
 
-from paged_decode.hybrid import allocate_hybrid_resources, decode_attention
+from paged_decode.hybrid import (HYBRID_BACKENDS, allocate_hybrid_resources, decode_attention,
+                                 validate_hybrid_options)
 from paged_decode.integration import configure_model
 from paged_decode.runtime import Resources
-from paged_decode.spec import DecodeSpec
+from paged_decode.spec import BACKENDS, DecodeSpec, validate_engine_options
 
 
 class FakeAttention(torch.nn.Module):
@@ -63,3 +66,19 @@ def test_hybrid_slot_resources_and_dispatch():
     with pytest.raises(ValueError, match="flash_attn"):
         decode_attention(None, None, None, None, None, backend="flash_attn", resources=None,
                          scale=0.0625)
+
+
+def test_matched_backend_belongs_to_the_fixed_batch_runner_only():
+    assert "triton_matched" in HYBRID_BACKENDS and "triton_matched" not in BACKENDS
+    with pytest.raises(ValueError, match="unknown decode_backend"):
+        validate_engine_options("triton_matched", 1, 256, 1, 1024)
+    validate_hybrid_options("triton_matched", "graph", 8, 2176)
+
+
+@pytest.mark.parametrize("options", [
+    ("unknown", "eager", 1, 1024), ("triton_matched", "unknown", 1, 1024),
+    ("triton_matched", "eager", 0, 1024), ("triton_matched", "eager", True, 1024),
+    ("triton_matched", "eager", 1, 0), ("triton_matched", "graph", 1, 2)])
+def test_invalid_runner_options(options):
+    with pytest.raises(ValueError):
+        validate_hybrid_options(*options)
