@@ -78,10 +78,12 @@ typedef enum PdlFlags {
   /* Lets pdl_paged_decode run ONE kernel: the CTA that finishes the last
    * partition of a (row, KV head) merges that group's partitions itself.
    * Used when the launch is short (at most 2 work items per CTA slot) and a
-   * group's partitions are small (splits * heads * head_dim * 4 <= 32 KB),
-   * where the second launch is a large share of the step; otherwise the
-   * library keeps the two-kernel path (the merge then starts early through
-   * programmatic dependent launch).  Needs `counters`, zero-initialised once; the
+   * group's partitions are small (splits * heads * head_dim * 4 <= 32 KB);
+   * otherwise the library keeps the two-kernel path.  Optional: measured on
+   * B200, the two-kernel path (merge launched programmatically, its rows
+   * staged through shared memory) is now the faster one (config 1: 6.7 vs
+   * 7.9 us per step; config 3, B=32: 50.3 vs 51.5 us), and this library's
+   * Python API no longer sets the flag.  Needs `counters`, zero-initialised once; the
    * kernel leaves it zeroed.  The workspace is still written and the output
    * is bit-identical to the two-kernel path. */
   PDL_FLAG_FUSED_MERGE = 4,

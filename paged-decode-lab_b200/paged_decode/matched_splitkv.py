@@ -24,9 +24,10 @@ class MatchedResources:
     out: torch.Tensor
     partials: torch.Tensor
     lse: torch.Tensor
-    # Group counters of the fused partition+merge kernel plus the two words of
-    # the dynamic scheduler (zeroed; the kernels leave them zeroed).  None
-    # selects the two-kernel launch with static scheduling.
+    # Scheduler words of the dynamically scheduled partition kernel (the two
+    # entries after batch*heads group counters, which only the optional fused
+    # merge uses); zeroed, left zeroed by the kernels.  None selects static
+    # scheduling.
     counters: torch.Tensor | None = None
 
 
@@ -86,8 +87,7 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
                            protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
                            partial=resources.partials, lse=resources.lse,
                            counters=resources.counters,
-                           flags=0 if resources.counters is None
-                           else ops.FLAG_FUSED_MERGE | ops.FLAG_DYNAMIC)
+                           flags=0 if resources.counters is None else ops.FLAG_DYNAMIC)
     ops.paged_decode(args, q.device)
     cache.put(key, args)
     return resources.out

@@ -34,8 +34,9 @@ class Resources:
     maxima: torch.Tensor | None = None
     denoms: torch.Tensor | None = None
     accums: torch.Tensor | None = None
-    # Group counters of the fused partition+merge kernel plus the dynamic
-    # scheduler's two words (zeroed, split backends only; left zeroed).
+    # Scheduler words of the dynamically scheduled partition kernel (the two
+    # entries after batch*heads group counters, which only the optional fused
+    # merge uses); zeroed, split backends only, left zeroed by the kernels.
     counters: torch.Tensor | None = None
 
 
@@ -169,8 +170,7 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
                                protocol=ops.PROTOCOL_MLA, kernel=kernel, out=resources.out,
                                maxima=resources.maxima, denoms=resources.denoms,
                                accums=resources.accums, counters=resources.counters,
-                               flags=0 if resources.counters is None
-                               else ops.FLAG_FUSED_MERGE | ops.FLAG_DYNAMIC)
+                               flags=0 if resources.counters is None else ops.FLAG_DYNAMIC)
     else:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)
