@@ -1,0 +1,51 @@
+"""CPU checks of the benchmark's output contract.
+
+The reference arm (``bench.py --impl reference``) times the CPU reference
+path and needs no GPU, so its JSON line is checked here key by key; under
+torchrun only rank 0 runs it and the other ranks exit 0 without work.  The
+GPU arm's line carries the same keys plus ``roofline``, ``clocks`` and
+``gpu_launches`` (exercised by the GPU runs, not here).
+"""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def run_bench(*args, env=None):
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True,
+                          text=True, timeout=600, env={**os.environ, **(env or {})}, cwd=ROOT)
+    lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
+    return proc.returncode, lines, proc.stderr
+
+
+def test_reference_arm_prints_one_contract_line():
+    rc, lines, err = run_bench("--impl", "reference", "--steps", "1", "--warmup", "1")
+    assert rc == 0, err[-2000:]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["higher_is_better"] is True
+    assert line["value"] > 0 and line["config"]["workload"] == "cfg2"
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"],
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    rc, lines, err = run_bench("--impl", "reference", "--steps", "1", "--warmup", "1",
+                               env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert rc == 0 and lines == [], err[-2000:]
+
+
+def test_exchange_micro_needs_several_ranks():
+    rc, lines, _ = run_bench("--exchange-micro")
+    assert rc == 0 and json.loads(lines[0]) == {
+        "exchange_micro": "needs torchrun with 2 or more ranks"}
