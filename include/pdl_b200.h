@@ -92,7 +92,9 @@ typedef enum PdlFlags {
    * instead of a static stride: balances batches of very different lengths.
    * Uses counters[batch*num_heads] and [batch*num_heads + 1] (so `counters`
    * needs batch*num_heads + 2 entries, zero-initialised once; the kernel
-   * leaves them zeroed).  Outputs are bit-identical to static scheduling. */
+   * leaves them zeroed).  Applied only when a launch has more work items than
+   * CTA slots (two per SM); one wave needs no scheduling.  Outputs are
+   * bit-identical to static scheduling. */
   PDL_FLAG_DYNAMIC = 8
 } PdlFlags;
 
