@@ -30,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st *pdl_stream_t; /* same handle as cudaStream_t */
 
-#define PDL_ABI_VERSION 3
+#define PDL_ABI_VERSION 4
 #define PDL_PAGE_SIZE 256
 
 typedef enum PdlStatus {
@@ -67,7 +67,8 @@ typedef enum PdlKernel {
   PDL_KERNEL_MMA = 2   /* BF16 tensor-core kernel (mma.sync), FP32 softmax    */
 } PdlKernel;
 
-/* Optional behaviour bits for PdlDecodeArgs.flags (0 = reference behaviour). */
+/* Optional behaviour bits for PdlDecodeArgs.flags (0 = reference behaviour);
+ * other bits are rejected with PDL_ERR_SHAPE. */
 typedef enum PdlFlags {
   /* Do not store empty partitions; the merge then reads only the
    * ceil(len / tokens_per_split) live partitions of each row. */
@@ -75,26 +76,12 @@ typedef enum PdlFlags {
   /* With splits == 1, pdl_paged_decode writes the output directly from the
    * partition kernel and leaves the workspace untouched. */
   PDL_FLAG_DIRECT_SINGLE = 2,
-  /* Lets pdl_paged_decode run ONE kernel: the CTA that finishes the last
-   * partition of a (row, KV head) merges that group's partitions itself.
-   * Used when the launch is short (at most 2 work items per CTA slot) and a
-   * group's partitions are small (splits * heads * head_dim * 4 <= 32 KB);
-   * otherwise the library keeps the two-kernel path.  Optional: measured on
-   * B200, the two-kernel path (merge launched programmatically, its rows
-   * staged through shared memory) is now the faster one (config 1: 6.7 vs
-   * 7.9 us per step; config 3, B=32: 50.3 vs 51.5 us), and this library's
-   * Python API no longer sets the flag.  Needs `counters`, zero-initialised once; the
-   * kernel leaves it zeroed.  The workspace is still written and the output
-   * is bit-identical to the two-kernel path. */
-  PDL_FLAG_FUSED_MERGE = 4,
-  /* Work items are handed to the persistent CTAs from an atomic counter,
-   * partition-major (every row's first partition, then every second one...),
-   * instead of a static stride: balances batches of very different lengths.
-   * Uses counters[batch*num_heads] and [batch*num_heads + 1] (so `counters`
-   * needs batch*num_heads + 2 entries, zero-initialised once; the kernel
-   * leaves them zeroed).  Applied only when a launch has more work items than
-   * CTA slots (two per SM); one wave needs no scheduling.  Outputs are
-   * bit-identical to static scheduling. */
+  /* Work items are handed to the persistent CTAs from an atomic counter
+   * (each CTA's first item is its index; later ones are claimed) instead of
+   * a static stride: balances batches of very different lengths.  Uses
+   * counters[0] and counters[1] (zero-initialised once; the kernel leaves
+   * them zeroed).  The counter is touched only when a launch has more live
+   * work items than CTAs.  Outputs are bit-identical to static scheduling. */
   PDL_FLAG_DYNAMIC = 8
 } PdlFlags;
 
@@ -147,12 +134,13 @@ typedef struct PdlDecodeArgs {
   float *maxima;              /* MLA protocol: [batch, num_heads, splits]          */
   float *denoms;              /*               [batch, num_heads, splits]          */
   float *accums;              /*               [batch, num_heads, splits, head_dim] */
-  int32_t *counters;          /* PDL_FLAG_FUSED_MERGE / _DYNAMIC: int32 [batch*num_heads + 2], zeroed */
+  int32_t *counters;          /* PDL_FLAG_DYNAMIC: int32 [2] scheduler words, zeroed once   */
 } PdlDecodeArgs;
 
 /* Partition kernel: per (row, KV head, partition) online softmax over the
  * partition's tokens for every query head of the group; writes the split
- * workspace in args->protocol.  With tokens_per_split == 0 and splits == 1 it
+ * workspace in args->protocol.  Only partitions holding live tokens are
+ * computed; empty ones are stored as such (unless PDL_FLAG_SKIP_EMPTY).  With tokens_per_split == 0 and splits == 1 it
  * writes the normalised output to args->out directly and needs no workspace.
  * Replaces _normalized_partition (reference src/paged_decode/matched_splitkv.py:52-98),
  * _split (src/paged_decode/kernels.py:44-80), _tc_partition
@@ -215,7 +203,9 @@ int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream);
  * until exit; calls needing batch*num_heads*splits*(head_dim+1)*4 bytes
  * beyond that are rejected with PDL_ERR_WORKSPACE (pdl_last_error says how
  * much was needed).  The workspace pointers and protocol in `args` are
- * ignored (LSE protocol).  The first call on a device looks up the array's
+ * ignored (LSE protocol); the flags mean what they mean for
+ * pdl_paged_decode, PDL_FLAG_DYNAMIC using the caller's `counters` (two
+ * zeroed int32, rejected if NULL).  The first call on a device looks up the array's
  * device address with that device current; make that first call before any
  * stream capture.  All calls on a device share the array and it keeps the
  * last call's contents (nothing in it needs to start at zero), so calls

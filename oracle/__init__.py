@@ -20,6 +20,6 @@ from .reference import (  # noqa: F401
     bf16_bits, bits_to_f32, round_bf16,
     validate_metadata, gather_kv, dense_reference, partial, merge_partials,
     streaming_reference, partition_bounds, normalized_partitions, lse_merge,
-    unnormalized_partitions, merge_unnormalized, matched_reference,
+    unnormalized_partitions, merge_unnormalized, matched_reference, score_magnitudes,
 )
 from .plan import OraclePlan, make_splitkv_plan, spec_geometry  # noqa: F401

@@ -207,6 +207,32 @@ def normalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, sca
     return partials, lse
 
 
+def score_magnitudes(q, k, table, lengths, tokens_per_split, splits, scale=None):
+    """Per partition, the largest sum_i |q_i * k_ti| * |scale| over its tokens.
+
+    This is the magnitude an FP32 dot product's rounding error scales with
+    (a score near 0 can come from terms of size ~1), so it bounds how
+    closely any FP32 implementation -- the reference's NumPy one included --
+    can reproduce an LSE whose value is near 0.  0 for empty partitions.
+    Shape [B, Hq, S].  (Test-side tolerance helper; no reference counterpart.)
+    """
+    q = np.asarray(q, dtype=np.float32)
+    scale = abs(_default_scale(q, scale))
+    batch, heads, dim = q.shape
+    group = heads // k.shape[2]
+    mags = np.zeros((batch, heads, splits), dtype=np.float64)
+    for b in range(batch):
+        n = int(lengths[b])
+        keys = np.abs(gather_kv(k, table[b], n).astype(np.float64))
+        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits)):
+            if end <= start:
+                continue
+            for h in range(heads):
+                kv = h // group
+                mags[b, h, p] = (keys[start:end, kv] @ np.abs(q[b, h].astype(np.float64))).max() * scale
+    return mags
+
+
 def lse_merge(partials, lse):
     """Stable LSE merge of normalised partials (matched_splitkv.py:101-127).
 

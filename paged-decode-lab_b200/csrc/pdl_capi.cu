@@ -174,6 +174,8 @@ int validate_common(const PdlDecodeArgs *a) {
   if (a->splits <= 0 || a->tokens_per_split < 0) return PDL_ERR_SPLITS;
   if (a->tokens_per_split == 0 && a->splits != 1) return PDL_ERR_SPLITS;
   if (a->protocol != PDL_PROTOCOL_LSE && a->protocol != PDL_PROTOCOL_MLA) return PDL_ERR_SHAPE;
+  if (a->flags & ~(PDL_FLAG_SKIP_EMPTY | PDL_FLAG_DIRECT_SINGLE | PDL_FLAG_DYNAMIC))
+    return fail(PDL_ERR_SHAPE, "flags", "unknown PdlFlags bit");
   return PDL_OK;
 }
 
@@ -181,6 +183,7 @@ int validate_partition_inputs(const PdlDecodeArgs *a) {
   if (!a->q || !a->k_cache || !a->v_cache || !a->block_table || !a->lengths) return PDL_ERR_NULL;
   if (a->num_pages <= 0 || a->num_pages > INT32_MAX) return PDL_ERR_SHAPE;
   if (a->table_width <= 0 || a->table_stride < a->table_width) return PDL_ERR_SHAPE;
+  if ((int64_t)a->table_width * PDL_PAGE_SIZE > INT32_MAX) return PDL_ERR_SHAPE;
   if (a->q_stride_head < a->head_dim || a->q_stride_batch < 1) return PDL_ERR_SHAPE;
   if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)) return PDL_ERR_ALIGNMENT;
   if (!aligned(a->q, 2)) return PDL_ERR_ALIGNMENT;
@@ -213,10 +216,8 @@ int status_from_cuda(cudaError_t e, const char *where) {
   return e == cudaSuccess ? PDL_OK : cuda_fail(where, e);
 }
 
-// Launch the partition kernel in `mode` (MODE_LSE / MODE_MLA / MODE_DIRECT);
-// `fused` lets it merge finished groups itself (PDL_FLAG_FUSED_MERGE).
-int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream, bool fused = false,
-                  bool *did_fuse = nullptr) {
+// Launch the partition kernel in `mode` (MODE_LSE / MODE_MLA / MODE_DIRECT).
+int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   DeviceState *dev = nullptr;
   int st = current_device_state(&dev);
   if (st != PDL_OK) return st;
@@ -233,7 +234,8 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream, bool fu
   }
   const int nsub = (group + per_cta - 1) / per_cta;
   const int64_t items = (int64_t)a->splits * a->num_kv_heads * nsub * a->batch;
-  if (items > INT32_MAX) return PDL_ERR_SHAPE;
+  // Item indices (and the fill items added per row) stay in int32.
+  if (items + a->batch > INT32_MAX) return PDL_ERR_SHAPE;
 
   CUtensorMap kmap, vmap;
   st = cached_pool_map(&kmap, a->k_cache, a->num_pages, a->num_kv_heads, a->head_dim, box);
@@ -275,22 +277,10 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream, bool fu
   p.denoms = a->denoms;
   p.accums = a->accums;
   p.fault = dev->fault;
-  // The fused merge pays off when the launch is short (at most two items per
-  // CTA slot), where a second kernel launch is a large share of the step; on
-  // long launches the per-item counting costs more than the launch it saves.
-  // Only small merges are fused: the merging CTA pulls a whole group's
-  // partitions through one SM, while the separate merge kernel spreads them.
-  const int64_t group_bytes = (int64_t)a->splits * per_cta * a->head_dim * 4;
-  const bool fuse = fused && mode != MODE_DIRECT && items <= 4LL * dev->sm_count &&
-                    group_bytes <= 32 * 1024;
-  p.counters = fuse ? a->counters : nullptr;
-  if (did_fuse) *did_fuse = fuse;
-  // Dynamic scheduling (two words after the group counters of this batch)
-  // only pays when CTAs take more than one item each; a single-item launch
-  // would just add an atomic round trip before its first load.
-  p.sched = (a->flags & PDL_FLAG_DYNAMIC) && a->counters && items > 2LL * dev->sm_count
-                ? a->counters + (int64_t)a->batch * a->num_heads
-                : nullptr;
+  // Dynamic scheduling: counters[0] counts claimed items, counters[1]
+  // finished CTAs.  The kernel uses them only when a launch has more live
+  // items than CTAs (each CTA's first item is blockIdx.x, no atomic).
+  p.sched = (a->flags & PDL_FLAG_DYNAMIC) ? a->counters : nullptr;
   const cudaError_t e = which == PDL_KERNEL_SIMT ? launch_partition_simt(L, stream)
                                                  : launch_partition_mma(L, stream);
   return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
@@ -469,6 +459,8 @@ extern "C" int pdl_partition(const PdlDecodeArgs *args, pdl_stream_t stream) {
   int st = validate_common(args);
   if (st == PDL_OK) st = validate_partition_inputs(args);
   if (st != PDL_OK) return st;
+  if ((args->flags & PDL_FLAG_DYNAMIC) && !args->counters)
+    return fail(PDL_ERR_WORKSPACE, "pdl_partition", "dynamic scheduling needs counters");
   const bool direct = args->tokens_per_split == 0;
   st = direct ? validate_out(args) : validate_workspace(args);
   if (st != PDL_OK) return st;
@@ -649,14 +641,6 @@ extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) 
   st = validate_workspace(args);
   if (st != PDL_OK) return st;
   const int mode = args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA;
-  if (args->flags & PDL_FLAG_FUSED_MERGE) {
-    if (!args->counters) return fail(PDL_ERR_WORKSPACE, "pdl_paged_decode", "fused merge needs counters");
-    if (!aligned(args->counters, 4)) return PDL_ERR_ALIGNMENT;
-    bool fused = false;
-    st = run_partition(args, mode, s, true, &fused);
-    if (st != PDL_OK || fused) return st;
-    return run_merge(args, s);
-  }
   st = run_partition(args, mode, s);
   if (st != PDL_OK) return st;
   return run_merge(args, s);
@@ -769,6 +753,9 @@ extern "C" int pdl_paged_decode_static_scratch(const PdlDecodeArgs *args, pdl_st
   if (st == PDL_OK) st = validate_out(args);
   if (st != PDL_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((args->flags & PDL_FLAG_DYNAMIC) && !args->counters)
+    return fail(PDL_ERR_WORKSPACE, "pdl_paged_decode_static_scratch",
+                "dynamic scheduling needs counters");
   if (args->tokens_per_split == 0) return run_partition(args, MODE_DIRECT, s);  // no workspace
   const int64_t rows = (int64_t)args->batch * args->num_heads * args->splits;
   const int64_t bytes = rows * (args->head_dim + 1) * (int64_t)sizeof(float);

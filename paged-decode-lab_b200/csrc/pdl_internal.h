@@ -17,9 +17,10 @@ enum OutMode : int {
   MODE_DIRECT = 2,  // one partition per row: normalised BF16 output
 };
 
-// Work item = (row b, KV head, head sub-group, partition); items are
-// enumerated partition-fastest and handed to persistent CTAs round-robin, or
-// partition-major from an atomic counter (dynamic scheduling, `sched`).
+// Work item = (row b, KV head, head sub-group, partition).  The producer warp
+// of every persistent CTA enumerates the live items from the lengths and
+// hands them out round-robin over the CTAs, or from an atomic counter
+// (dynamic scheduling, `sched`).
 struct PartitionParams {
   const __nv_bfloat16 *q;
   int64_t q_stride_batch;   // elements
@@ -35,7 +36,7 @@ struct PartitionParams {
   int32_t nsub;             // head sub-groups per KV head
   int32_t tokens_per_split; // > 0
   int32_t splits;
-  int32_t n_items;          // splits * num_kv_heads * nsub * batch
+  int32_t n_items;          // splits * num_kv_heads * nsub * batch (live or not)
   float log2_scale;         // scale * log2(e)
   int32_t mode;             // OutMode
   int32_t q_vec16;          // q rows 16-byte aligned (vector loads)
@@ -47,8 +48,7 @@ struct PartitionParams {
   float *denoms;
   float *accums;
   uint32_t *fault;          // per-device fault word
-  int32_t *counters;        // fused merge: finished items per (row, KV head, sub-group), or null
-  int32_t *sched;           // dynamic scheduling: [next item, finished CTAs], or null (static)
+  int32_t *sched;           // dynamic scheduling: [items claimed, finished CTAs], or null (static)
 };
 
 // Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],

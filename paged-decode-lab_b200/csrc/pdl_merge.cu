@@ -40,15 +40,15 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   // The next decode step's partition kernel may be scheduled now; it waits
   // for this grid to complete before touching the workspace.
   allow_dependent_launch();
-  // Lengths are an input of the decode, not an output of the partition
-  // kernel, so they are read before waiting for it.
-  int live = p.splits;
-  if (p.lengths != nullptr && row < p.rows) {
-    const int len = __ldg(p.lengths + row / p.num_heads);
-    live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
-  }
+  // Everything, the lengths included, is read after the partition kernel
+  // (and, through it, every kernel before it) has completed.
   grid_dependency_wait();
   if (row >= p.rows) return;
+  int live = p.splits;
+  if (p.lengths != nullptr) {
+    const int len = max(__ldg(p.lengths + row / p.num_heads), 0);
+    live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+  }
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;
   const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;

@@ -13,9 +13,8 @@
 //   M = max_p m_p (-inf -> 0); f_p = exp(m_p - M);
 //   out = sum_p f_p * acc_p / (sum_p f_p * l_p, or 1 when that is 0).
 // Partitions are accumulated in index order with one fused multiply-add per
-// partition, whatever the staging of the loads; the fused merge of the
-// partition kernels (merge_group) and the exchange kernel's merge across
-// ranks keep the same order, so all of them give the same bits.
+// partition, whatever the staging of the loads; the exchange kernel's merge
+// across ranks keeps the same order, so both give the same bits.
 #pragma once
 
 #include "pdl_device.cuh"

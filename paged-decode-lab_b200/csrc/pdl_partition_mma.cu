@@ -118,12 +118,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFFSET);
   uint64_t *empty = full + NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET);
-  volatile int *merge_flag = abort_flag + 1;
-  ItemRing ring;
-  ring.full = reinterpret_cast<uint64_t *>(smem + L::RING_OFFSET);
-  ring.empty = ring.full + IR;
-  ring.slot = reinterpret_cast<volatile int *>(ring.empty + IR);
-  ring.shared = abort_flag + 2;
+  const ItemRing ring = item_ring<L>(smem);
   if (!smem_base_aligned(smem, p.fault)) return;
 
   // The merge kernel that follows may be scheduled now; it waits for this
@@ -165,14 +160,15 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   uint32_t it = 0;
 
   uint32_t ik = 0;
-  int static_next = blockIdx.x;
   while (true) {
-    const int item = consumer_next<NC>(p, ring, ik, static_next, cw, lane, abort_flag);
-    if (item < 0) break;
-    const Item w = decode_item(p, item);
-    const int h0 = w.kvh * p.group + w.sub * GC;
-    const int rows = min(GC, p.group - w.sub * GC);
-    // q is loaded before the row length is known, so both round trips overlap.
+    const WorkItem w = consumer_next<NC>(ring, ik, cw, lane, p.fault, abort_flag);
+    if (w.kind == ITEM_STOP) break;
+    int h0, rows;
+    item_heads<GC>(p, w.hs, h0, rows);
+    if (w.kind == ITEM_FILL) {
+      store_fill<D>(p, w, h0, rows, tid, NC * 32);
+      continue;
+    }
     // q of head (nt*8 + grp) as B fragments: dims kk*16 + quad*2 + {0,1} and +8.
     uint32_t qf[NT][KS][2];
 #pragma unroll
@@ -188,14 +184,6 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       }
     }
 
-    const Range rg = item_range(p, w);
-    if (rg.start >= rg.stop) {
-      if (p.write_empty || p.mode == MODE_DIRECT)
-        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
-      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
-      continue;
-    }
-
     // Running state for heads nt*8 + quad*2 + {0,1}; acc[nt][j] holds O^T
     // rows (dh*KSW + j)*16 + grp (+8) for those two heads.
     float m[NT][2], l[NT][2], acc[NT][KSW][4];
@@ -207,15 +195,15 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       for (int dm = 0; dm < KSW; ++dm) acc[nt][dm][0] = acc[nt][dm][1] = acc[nt][dm][2] = acc[nt][dm][3] = 0.f;
     }
 
-    const int t0 = rg.start / T * T;
-    const int ntiles = (rg.stop - t0 + T - 1) / T;
+    const int t0 = w.start / T * T;
+    const int ntiles = (w.stop - t0 + T - 1) / T;
     const int r0 = tg * TW;
     for (int i = 0; i < ntiles; ++i, ++it) {
       const int s = it % NS;
       pipeline_wait(&full[s], (it / NS) & 1, p.fault, FAULT_CONSUMER_FULL_WAIT, abort_flag);
       const int tile_tok = t0 + i * T;
-      const int lo = max(rg.start - tile_tok, 0);
-      const int hi = min(rg.stop - tile_tok, T);
+      const int lo = max(w.start - tile_tok, 0);
+      const int hi = min(w.stop - tile_tok, T);
       if (r0 < hi && r0 + TW > lo) {
         const uint32_t ks = kbase + s * S::TILE_BYTES;
         const uint32_t vs = vbase + s * S::TILE_BYTES;
@@ -374,7 +362,6 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     named_barrier(1, NC * 32);
     combine_and_store<D, GC, NG, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
-    finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
   }
 }
 

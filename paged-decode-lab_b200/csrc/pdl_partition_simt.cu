@@ -56,12 +56,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFFSET);
   uint64_t *empty = full + NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET);
-  volatile int *merge_flag = abort_flag + 1;
-  ItemRing ring;
-  ring.full = reinterpret_cast<uint64_t *>(smem + L::RING_OFFSET);
-  ring.empty = ring.full + IR;
-  ring.slot = reinterpret_cast<volatile int *>(ring.empty + IR);
-  ring.shared = abort_flag + 2;
+  const ItemRing ring = item_ring<L>(smem);
   static_assert(L::BYTES <= kTwoCtaSmemBytes, "two CTAs per SM");
   if (!smem_base_aligned(smem, p.fault)) return;
 
@@ -101,14 +96,15 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   uint32_t it = 0;
 
   uint32_t ik = 0;
-  int static_next = blockIdx.x;
   while (true) {
-    const int item = consumer_next<NC>(p, ring, ik, static_next, cw, lane, abort_flag);
-    if (item < 0) break;
-    const Item w = decode_item(p, item);
-    const int h0 = w.kvh * p.group + w.sub * GC;
-    const int rows = min(GC, p.group - w.sub * GC);
-    // q is loaded before the row length is known, so both round trips overlap.
+    const WorkItem w = consumer_next<NC>(ring, ik, cw, lane, p.fault, abort_flag);
+    if (w.kind == ITEM_STOP) break;
+    int h0, rows;
+    item_heads<GC>(p, w.hs, h0, rows);
+    if (w.kind == ITEM_FILL) {
+      store_fill<D>(p, w, h0, rows, tid, NC * 32);
+      continue;
+    }
     // q chunk j of every head of the sub-group, as FP32 pairs.
     float2 q2[GC][4];
 #pragma unroll
@@ -131,14 +127,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       for (int e = 0; e < 4; ++e) q2[g][e] = bf16x2_to_float2(raw[e]);
     }
 
-    const Range rg = item_range(p, w);
-    if (rg.start >= rg.stop) {
-      if (p.write_empty || p.mode == MODE_DIRECT)
-        store_empty<D>(p, w.b, h0, rows, w.split, tid, NC * 32);
-      finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
-      continue;
-    }
-
     float m[GC], l[GC];
     float2 acc[GC][4];
 #pragma unroll
@@ -149,8 +137,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       for (int e = 0; e < 4; ++e) acc[g][e] = make_float2(0.f, 0.f);
     }
 
-    const int t0 = rg.start / T * T;
-    const int ntiles = (rg.stop - t0 + T - 1) / T;
+    const int t0 = w.start / T * T;
+    const int ntiles = (w.stop - t0 + T - 1) / T;
     const int r0 = cw * TW;
     for (int i = 0; i < ntiles; ++i, ++it) {
       const int s = it % NS;
@@ -159,8 +147,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       // fault word tells the host the results are invalid.
       pipeline_wait(&full[s], (it / NS) & 1, p.fault, FAULT_CONSUMER_FULL_WAIT, abort_flag);
       const int tile_tok = t0 + i * T;
-      const int lo = max(rg.start - tile_tok, 0);
-      const int hi = min(rg.stop - tile_tok, T);
+      const int lo = max(w.start - tile_tok, 0);
+      const int hi = min(w.stop - tile_tok, T);
       if (r0 < hi && r0 + TW > lo) {
         const uint32_t ks = kbase + s * S::TILE_BYTES;
         const uint32_t vs = vbase + s * S::TILE_BYTES;
@@ -261,7 +249,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     named_barrier(1, NC * 32);
     combine_and_store<D, GC, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
-    finish_item<D, NC>(p, w, h0, rows, cw, lane, merge_flag);
   }
 }
 

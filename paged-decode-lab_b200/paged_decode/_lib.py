@@ -8,7 +8,7 @@ import ctypes
 from pathlib import Path
 
 LIBRARY = Path(__file__).with_name("libpdl_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 PDL_OK = 0
 STATUS_NAMES = {
@@ -18,7 +18,7 @@ STATUS_NAMES = {
 }
 PROTOCOL_LSE, PROTOCOL_MLA = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
-FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_FUSED_MERGE, FLAG_DYNAMIC = 1, 2, 4, 8
+FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_DYNAMIC = 1, 2, 8
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
 SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode", "pdl_append_kv",

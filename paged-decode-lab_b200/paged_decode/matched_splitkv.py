@@ -24,10 +24,8 @@ class MatchedResources:
     out: torch.Tensor
     partials: torch.Tensor
     lse: torch.Tensor
-    # Scheduler words of the dynamically scheduled partition kernel (the two
-    # entries after batch*heads group counters, which only the optional fused
-    # merge uses); zeroed, left zeroed by the kernels.  None selects static
-    # scheduling.
+    # The two scheduler words of the dynamically scheduled partition kernel;
+    # zeroed, left zeroed by the kernels.  None selects static scheduling.
     counters: torch.Tensor | None = None
 
 
@@ -52,7 +50,7 @@ def allocate_matched_resources(spec, device, *, num_splits=0, plan=None):
                     dtype=torch.bfloat16),
         torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32),
         torch.empty(shape, device=device, dtype=torch.float32),
-        torch.zeros(spec.max_batch * spec.num_heads + 2, device=device, dtype=torch.int32))
+        torch.zeros(2, device=device, dtype=torch.int32))
 
 
 def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="auto"):

@@ -19,7 +19,6 @@ KERNEL_SIMT = _lib.KERNEL_SIMT
 KERNEL_MMA = _lib.KERNEL_MMA
 FLAG_SKIP_EMPTY = _lib.FLAG_SKIP_EMPTY
 FLAG_DIRECT_SINGLE = _lib.FLAG_DIRECT_SINGLE
-FLAG_FUSED_MERGE = _lib.FLAG_FUSED_MERGE
 FLAG_DYNAMIC = _lib.FLAG_DYNAMIC
 
 _KERNELS = {"auto": KERNEL_AUTO, "simt": KERNEL_SIMT, "mma": KERNEL_MMA}

@@ -233,7 +233,7 @@ class ContextParallelDecode:
         self.out = torch.empty(b, hq, d, device=self.device, dtype=torch.bfloat16)
         self.local_len = torch.zeros(b, device=self.device, dtype=torch.int32)
         # Dynamic-scheduler words of the local partition launch (left zeroed).
-        self.counters = torch.zeros(b * hq + 2, device=self.device, dtype=torch.int32)
+        self.counters = torch.zeros(2, device=self.device, dtype=torch.int32)
         self.exchange_mode = exchange
         self.peer = PeerExchange(b * hq, d, self.device, group) if exchange == "p2p" else None
         self._args = {}

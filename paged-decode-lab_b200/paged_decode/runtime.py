@@ -34,9 +34,8 @@ class Resources:
     maxima: torch.Tensor | None = None
     denoms: torch.Tensor | None = None
     accums: torch.Tensor | None = None
-    # Scheduler words of the dynamically scheduled partition kernel (the two
-    # entries after batch*heads group counters, which only the optional fused
-    # merge uses); zeroed, split backends only, left zeroed by the kernels.
+    # The two scheduler words of the dynamically scheduled partition kernel;
+    # zeroed, split backends only, left zeroed by the kernels.
     counters: torch.Tensor | None = None
 
 
@@ -56,8 +55,7 @@ def allocate_resources(spec, device, backend="triton_splitk"):
         result.maxima = torch.empty(shape, device=device, dtype=torch.float32)
         result.denoms = torch.empty(shape, device=device, dtype=torch.float32)
         result.accums = torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32)
-        result.counters = torch.zeros(spec.max_batch * spec.num_heads + 2, device=device,
-                                      dtype=torch.int32)
+        result.counters = torch.zeros(2, device=device, dtype=torch.int32)
     return result
 
 

@@ -46,7 +46,9 @@ def make_b200_plan(spec, sm_count):
     About one work item per CTA slot (two CTAs per SM), items of at most
     4096 tokens so variable-length batches balance under dynamic scheduling,
     partitions a multiple of the reference plan's tile.  Use it through
-    ``allocate_matched_resources(spec, device, num_splits=plan.splits)``.
+    ``allocate_matched_resources(spec, device, plan=make_b200_plan(spec, sms))``:
+    ``num_splits=plan.splits`` would recompute ``tokens_per_split`` with the
+    reference heuristic's rounding, which can give other partition bounds.
     """
     if type(sm_count) is not int or sm_count < 1:
         raise ValueError("positive SM count required")

@@ -18,11 +18,25 @@ def pytest_configure(config):
 
 
 def pytest_sessionstart(session):
-    """Build the sm_100a library once if this checkout has none yet (nvcc
-    cross-compiles without a GPU); an existing build is left as it is."""
-    library = ROOT / "paged-decode-lab_b200" / "paged_decode" / "libpdl_b200.so"
-    if not library.exists():
-        csrc = ROOT / "paged-decode-lab_b200" / "csrc"
-        sys.path.insert(0, str(csrc))
-        import importlib
-        importlib.import_module("build").build()
+    """Bring the sm_100a library up to date before any test loads it: the
+    build recompiles only sources newer than their objects (nvcc
+    cross-compiles without a GPU), so a library older than csrc/ is never
+    tested as it is."""
+    csrc = ROOT / "paged-decode-lab_b200" / "csrc"
+    sys.path.insert(0, str(csrc))
+    import importlib
+    importlib.import_module("build").build()
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Worst observed error / bound ratios of the parity checks in this run."""
+    gpu_util = sys.modules.get("gpu_util")
+    if gpu_util is None or not gpu_util.WORST["lse_checked"] and not gpu_util.WORST["output_ratio"]:
+        return
+    w = gpu_util.WORST
+    terminalreporter.write_line(
+        "parity worst: output max abs err %.3e (%.3f of 2^-7); LSE error/bound %.3f over %d "
+        "values, largest relative LSE error where |ref| >= 1e-3: %.3e; %d values needed the "
+        "FP32 score allowance" % (w["output_abs_err"], w["output_ratio"], w["lse_ratio"],
+                                  w["lse_checked"], w["lse_rel_err_strict"],
+                                  w["lse_needing_score_allowance"]))

@@ -1,22 +1,40 @@
 """Helpers for the GPU parity tests: device copies of seeded cases and the
 tolerances of the parity contract.
 
-Tolerances (north-star contract, checked against the NumPy oracle on the
+Tolerances (the north-star contract, checked against the NumPy oracle on the
 same BF16 bits):
-  * output: |gpu - ref| <= 2^-7 + 2^-8 * |ref|  -- max-abs 2^-7, plus the
-    half-ulp rounding of the BF16 output itself for |ref| > 1;
-  * LSE:    |gpu - ref| <= 1e-5 * max(1, |ref|), and -inf exactly where the
-    oracle has -inf (empty partitions);
+  * output: max |gpu - ref| <= 2^-7.
+  * LSE:    |gpu - ref| <= 1e-5 * |ref|, with an absolute floor of
+    1e-5 * 1e-3 where |ref| < 1e-3; -inf exactly where the oracle has -inf
+    (empty partitions).  Where the caller passes the partition's score
+    magnitude S (oracle.score_magnitudes: the largest sum_i |q_i k_i| * scale
+    over its tokens), the bound is at least SCORE_ULPS * 2^-24 * (S + 1).
+    Why: a partition's LSE is 1-Lipschitz in its scores, and an FP32 score
+    (any FP32 dot product: the GPU's, the NumPy reference's) is rounded on
+    the scale of S, not of its value; ln l adds the rounding of ex2/log2 on
+    the scale of 1.  A partition of one or two tokens whose score is near 0
+    therefore cannot be reproduced to 1e-5 *relative* by any FP32
+    implementation; everywhere else the relative bound is what binds.
   * page addressing and partition bounds: bit-exact (checked through
     bit-identical outputs under page relocation and split re-layout).
+
+The worst observed ratios (error / bound) of a session are kept in WORST and
+printed at the end of the run (tests/conftest.py).
 """
 import numpy as np
 import pytest
 import torch
 
 OUT_ATOL = 2.0 ** -7
-OUT_RTOL = 2.0 ** -8
 LSE_RTOL = 1e-5
+LSE_FLOOR_BELOW = 1e-3
+SCORE_ULPS = 8
+U32 = 2.0 ** -24
+
+# Worst (error / bound) ratios seen in this session, plus the largest
+# relative LSE error where |ref| >= 1e-3 and no score allowance was needed.
+WORST = {"output_abs_err": 0.0, "output_ratio": 0.0, "lse_ratio": 0.0,
+         "lse_rel_err_strict": 0.0, "lse_checked": 0, "lse_needing_score_allowance": 0}
 
 requires_cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
 
@@ -34,26 +52,51 @@ def device_case(case, device="cuda"):
             torch.from_numpy(np.ascontiguousarray(case.lengths)).to(device))
 
 
+def _np(x):
+    return x.float().cpu().numpy() if torch.is_tensor(x) else np.asarray(x, dtype=np.float32)
+
+
 def assert_out_close(actual, expected, what="output"):
-    a = actual.float().cpu().numpy() if torch.is_tensor(actual) else np.asarray(actual)
-    e = expected.float().cpu().numpy() if torch.is_tensor(expected) else np.asarray(expected)
+    a, e = _np(actual), _np(expected)
     assert a.shape == e.shape, (a.shape, e.shape)
     assert np.isfinite(a).all(), f"{what}: non-finite values"
     err = np.abs(a - e)
-    bound = OUT_ATOL + OUT_RTOL * np.abs(e)
-    worst = np.unravel_index(np.argmax(err - bound), err.shape)
-    assert (err <= bound).all(), (f"{what}: max abs err {err.max():.3e}; worst at {worst}: "
-                                  f"got {a[worst]}, want {e[worst]}")
-    return float(err.max())
+    worst = float(err.max(initial=0.0))
+    WORST["output_abs_err"] = max(WORST["output_abs_err"], worst)
+    WORST["output_ratio"] = max(WORST["output_ratio"], worst / OUT_ATOL)
+    at = np.unravel_index(np.argmax(err), err.shape) if err.size else ()
+    assert worst <= OUT_ATOL, (f"{what}: max abs err {worst:.3e} > 2^-7 at {at}: "
+                               f"got {a[at]}, want {e[at]}")
+    return worst
 
 
-def assert_lse_close(actual, expected, what="lse"):
-    a = actual.float().cpu().numpy() if torch.is_tensor(actual) else np.asarray(actual)
-    e = np.asarray(expected, dtype=np.float32)
+def lse_bound(expected, score_mag=None):
+    e = np.abs(np.asarray(expected, dtype=np.float64))
+    bound = LSE_RTOL * np.maximum(e, LSE_FLOOR_BELOW)
+    if score_mag is not None:
+        bound = np.maximum(bound, SCORE_ULPS * U32 * (np.asarray(score_mag, np.float64) + 1.0))
+    return bound
+
+
+def assert_lse_close(actual, expected, what="lse", score_mag=None):
+    a = _np(actual).astype(np.float64)
+    e = np.asarray(_np(expected), dtype=np.float64)
     assert a.shape == e.shape, (a.shape, e.shape)
     np.testing.assert_array_equal(np.isneginf(a), np.isneginf(e), err_msg=f"{what}: -inf layout")
     fin = np.isfinite(e)
     assert np.isfinite(a[fin]).all()
     err = np.abs(a[fin] - e[fin])
-    bound = LSE_RTOL * np.maximum(1.0, np.abs(e[fin]))
-    assert (err <= bound).all(), f"{what}: max rel err {(err / np.maximum(1, np.abs(e[fin]))).max():.3e}"
+    mag = None if score_mag is None else np.asarray(score_mag)[fin]
+    bound = lse_bound(e[fin], mag)
+    strict = LSE_RTOL * np.maximum(np.abs(e[fin]), LSE_FLOOR_BELOW)
+    if err.size:
+        WORST["lse_checked"] += int(err.size)
+        WORST["lse_ratio"] = max(WORST["lse_ratio"], float((err / bound).max()))
+        WORST["lse_needing_score_allowance"] += int((err > strict).sum())
+        big = np.abs(e[fin]) >= LSE_FLOOR_BELOW
+        if big.any():
+            WORST["lse_rel_err_strict"] = max(WORST["lse_rel_err_strict"],
+                                              float((err[big] / np.abs(e[fin][big])).max()))
+    bad = err > bound
+    assert not bad.any(), (f"{what}: {int(bad.sum())} LSE values outside the bound; worst "
+                           f"|err| {err.max():.3e} at |ref| {np.abs(e[fin])[np.argmax(err / bound)]:.3e}")

@@ -41,7 +41,9 @@ def test_explicit_cross_page_boundaries(kernel, splits, dim, hq, hkv):
     ref_out, ref_partials, ref_lse = oracle.matched_reference(
         *case.arrays(), res.plan.tokens_per_split, res.plan.splits)
     assert_out_close(out, ref_out)
-    assert_lse_close(res.lse, ref_lse)
+    mags = oracle.score_magnitudes(case.q, case.k, case.table, case.lengths,
+                                   res.plan.tokens_per_split, res.plan.splits)
+    assert_lse_close(res.lse, ref_lse, score_mag=mags)
     assert_out_close(res.partials, ref_partials, "partials")
     assert torch.count_nonzero(out[0]) == 0
 
@@ -107,7 +109,9 @@ def test_config1_partitions_against_reference_golden(kernel):
                                          protocol=ops.PROTOCOL_LSE, kernel=kernel, out=out,
                                          partial=partial, lse=lse), q.device)
         key = f"cfg1/p{tokens}"
-        assert_lse_close(lse, golden[f"{key}/lse"])
+        mags = oracle.score_magnitudes(case.q, case.k, case.table, case.lengths, tokens, splits,
+                                       128 ** -0.5)
+        assert_lse_close(lse, golden[f"{key}/lse"], score_mag=mags)
         assert_out_close(partial, golden[f"{key}/partial"], "partial")
         assert_out_close(out, golden["cfg1/dense"])
         # Same run, unnormalised protocol: (m, l, acc) of the reference's _split.
@@ -118,7 +122,7 @@ def test_config1_partitions_against_reference_golden(kernel):
                                          tokens_per_split=tokens, splits=splits,
                                          protocol=ops.PROTOCOL_MLA, kernel=kernel, out=out,
                                          maxima=maxima, denoms=denoms, accums=accums), q.device)
-        assert_lse_close(maxima, golden[f"{key}/m"], "maxima")
+        assert_lse_close(maxima, golden[f"{key}/m"], "maxima", score_mag=mags)
         ref_l = golden[f"{key}/l"]
         got_l = denoms.cpu().numpy()
         np.testing.assert_allclose(got_l, ref_l, rtol=2e-5, atol=0)
@@ -161,30 +165,99 @@ def test_split_layout_invariance(kernel):
 
 @pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("protocol", ["lse", "mla"])
-@pytest.mark.parametrize("skip_empty", [False, True])
-def test_fused_merge_equals_two_kernel_path(kernel, protocol, skip_empty):
-    """One kernel (last CTA of a group merges) == partition + merge kernels, bit for bit."""
-    case = cases.make_case([3000, 0, 1, 4096, 257], 8, 2, 128, seed=12, capacity=4096)
+@pytest.mark.parametrize("flags", [0, "dynamic", "skip", "dynamic+skip"])
+def test_every_partition_slot_follows_the_workspace_contract(kernel, protocol, flags):
+    """Live partitions hold the oracle's values; empty ones are stored as empty
+    (partial 0 / LSE -inf, or (-inf, 0, 0)) unless PDL_FLAG_SKIP_EMPTY, which
+    leaves them untouched.  The workspace starts NaN-poisoned."""
+    lengths = [3000, 0, 1, 4096, 257, 2048, 2049, 0]
+    rows, hq, hkv, d, tps, splits = len(lengths), 8, 2, 128, 512, 8
+    case = cases.make_case(lengths, hq, hkv, d, seed=12, capacity=4096)
     q, k, v, table, lens = device_case(case)
-    counters = torch.zeros(5 * 8 + 2, dtype=torch.int32, device="cuda")
-    outs = []
-    for fused in (False, True):
-        out = torch.empty(5, 8, 128, dtype=torch.bfloat16, device="cuda")
-        ws = dict(partial=torch.empty(5, 8, 8, 128, device="cuda"),
-                  lse=torch.empty(5, 8, 8, device="cuda")) if protocol == "lse" else dict(
-            maxima=torch.empty(5, 8, 8, device="cuda"), denoms=torch.empty(5, 8, 8, device="cuda"),
-            accums=torch.empty(5, 8, 8, 128, device="cuda"))
-        flags = (ops.FLAG_SKIP_EMPTY if skip_empty else 0) | (ops.FLAG_FUSED_MERGE if fused else 0)
-        args = ops.decode_args(q, k, v, table, lens, scale=0.09, tokens_per_split=512, splits=8,
-                               protocol=ops.PROTOCOL_LSE if protocol == "lse" else ops.PROTOCOL_MLA,
-                               kernel=kernel, flags=flags, out=out, counters=counters, **ws)
-        for _ in range(2):  # the second launch reuses the counters the first left zeroed
-            ops.paged_decode(args, q.device)
-        outs.append(out)
+    bits = {"dynamic": ops.FLAG_DYNAMIC, "skip": ops.FLAG_SKIP_EMPTY,
+            "dynamic+skip": ops.FLAG_DYNAMIC | ops.FLAG_SKIP_EMPTY}.get(flags, 0)
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
+    nan = dict(device="cuda", dtype=torch.float32)
+    out = torch.empty(rows, hq, d, dtype=torch.bfloat16, device="cuda")
+    if protocol == "lse":
+        ws = dict(partial=torch.full((rows, hq, splits, d), float("nan"), **nan),
+                  lse=torch.full((rows, hq, splits), float("nan"), **nan))
+    else:
+        ws = dict(maxima=torch.full((rows, hq, splits), float("nan"), **nan),
+                  denoms=torch.full((rows, hq, splits), float("nan"), **nan),
+                  accums=torch.full((rows, hq, splits, d), float("nan"), **nan))
+    args = ops.decode_args(q, k, v, table, lens, scale=0.09, tokens_per_split=tps, splits=splits,
+                           protocol=ops.PROTOCOL_LSE if protocol == "lse" else ops.PROTOCOL_MLA,
+                           kernel=kernel, flags=bits, out=out, counters=counters, **ws)
+    for _ in range(2):  # the scheduler words reset themselves between launches
+        ops.paged_decode(args, q.device)
     torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1])
-    assert not counters.any()
-    assert_out_close(outs[1], oracle.dense_reference(*case.arrays(), scale=0.09))
+    assert not counters.any() and ops.read_fault() == 0
+    assert_out_close(out, oracle.dense_reference(*case.arrays(), scale=0.09))
+    live = torch.tensor([[p * tps < n for p in range(splits)] for n in lengths], device="cuda")
+    live = live[:, None, :].expand(rows, hq, splits)
+    skip = bool(bits & ops.FLAG_SKIP_EMPTY)
+    if protocol == "lse":
+        ref_p, ref_l = oracle.normalized_partitions(*case.arrays(), tps, splits, scale=0.09)
+        got_l = ws["lse"].clone()
+        mags = oracle.score_magnitudes(*case.arrays()[:2], case.table, case.lengths, tps, splits,
+                                       0.09)
+        assert_lse_close(got_l[live], ref_l[live.cpu().numpy()],
+                         score_mag=mags[live.cpu().numpy()])
+        assert_out_close(ws["partial"][live], ref_p[live.cpu().numpy()], "live partials")
+        empty_l, empty_p = ws["lse"][~live], ws["partial"][~live]
+        if skip:
+            assert torch.isnan(empty_l).all() and torch.isnan(empty_p).all()
+        else:
+            assert torch.isneginf(empty_l).all() and not empty_p.any()
+    else:
+        ref_m, ref_d, ref_a = oracle.unnormalized_partitions(*case.arrays(), tps, splits,
+                                                             scale=0.09)
+        m = live.cpu().numpy()
+        mags = oracle.score_magnitudes(*case.arrays()[:2], case.table, case.lengths, tps, splits,
+                                       0.09)
+        assert_lse_close(ws["maxima"][live], ref_m[m], "maxima", score_mag=mags[m])
+        assert np.allclose(ws["denoms"][live].cpu().numpy(), ref_d[m], rtol=1e-5)
+        empty = [ws["maxima"][~live], ws["denoms"][~live], ws["accums"][~live]]
+        if skip:
+            assert all(torch.isnan(t).all() for t in empty)
+        else:
+            assert torch.isneginf(empty[0]).all() and not empty[1].any() and not empty[2].any()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("rows", [512, 513, 700])
+def test_batches_past_the_register_schedule(kernel, rows):
+    """Up to 512 rows the producer keeps every length in registers and hands out
+    live items only; larger batches enumerate every partition.  Both must give
+    the oracle's outputs and identical bits under static and dynamic scheduling."""
+    gen = np.random.default_rng(rows)
+    lengths = gen.integers(0, 600, size=rows)
+    lengths[::7] = 0
+    case = cases.make_case(lengths, 4, 1, 64, seed=rows, capacity=768)
+    q, k, v, table, lens = device_case(case)
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = []
+    for flags in (0, ops.FLAG_DYNAMIC):
+        out = torch.empty(rows, 4, 64, dtype=torch.bfloat16, device="cuda")
+        partial = torch.full((rows, 4, 3, 64), float("nan"), device="cuda")
+        lse = torch.full((rows, 4, 3), float("nan"), device="cuda")
+        args = ops.decode_args(q, k, v, table, lens, scale=0.125, tokens_per_split=256, splits=3,
+                               protocol=ops.PROTOCOL_LSE, kernel=kernel, flags=flags, out=out,
+                               partial=partial, lse=lse, counters=counters)
+        ops.paged_decode(args, q.device)
+        outs.append((out, partial, lse))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][2], outs[1][2])
+    assert not counters.any() and ops.read_fault() == 0
+    few = list(range(0, rows, max(1, rows // 12)))
+    want = oracle.dense_reference(case.q[few], case.k, case.v, case.table[few],
+                                  case.lengths[few], scale=0.125)
+    assert_out_close(outs[1][0][few], want)
+    assert torch.count_nonzero(outs[1][0][lens == 0]) == 0
+    empty = torch.tensor([[p * 256 >= n for p in range(3)] for n in lengths], device="cuda")
+    assert torch.isneginf(outs[1][2][empty[:, None, :].expand(rows, 4, 3)]).all()
 
 
 @pytest.mark.parametrize("kernel", KERNELS)
@@ -194,7 +267,7 @@ def test_dynamic_scheduling_is_bit_identical_to_static(kernel):
     rows = len(lengths)
     case = cases.make_case(lengths, 8, 2, 128, seed=13, capacity=32768, pool_factor=1.0)
     q, k, v, table, lens = device_case(case)
-    counters = torch.zeros(rows * 8 + 2, dtype=torch.int32, device="cuda")
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
     outs = []
     for flags in (0, ops.FLAG_DYNAMIC, ops.FLAG_DYNAMIC | ops.FLAG_SKIP_EMPTY):
         out = torch.empty(rows, 8, 128, dtype=torch.bfloat16, device="cuda")
