@@ -270,6 +270,9 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   p.mode = mode;
   p.q_vec16 = aligned(a->q, 16) && (a->q_stride_batch % 8 == 0) && (a->q_stride_head % 8 == 0);
   p.write_empty = (a->flags & PDL_FLAG_SKIP_EMPTY) ? 0 : 1;
+  // A fill item stores about 16 KB: whole empty partitions of all heads of a row.
+  p.fill_splits =
+      (int)std::max<int64_t>(1, 16384 / ((int64_t)a->num_heads * (a->head_dim + 1) * 4));
   p.out = static_cast<__nv_bfloat16 *>(a->out);
   p.partial = a->partial;
   p.lse = a->lse;
@@ -286,7 +289,10 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
 }
 
-int run_merge(const PdlDecodeArgs *a, cudaStream_t stream) {
+// `after_partition`: the launch directly follows this library's partition
+// kernel on the stream (pdl_paged_decode), so the merge may read the lengths
+// before its dependency wait.
+int run_merge(const PdlDecodeArgs *a, cudaStream_t stream, bool after_partition) {
   MergeParams m;
   std::memset(&m, 0, sizeof(m));
   m.partial = a->partial;
@@ -298,6 +304,7 @@ int run_merge(const PdlDecodeArgs *a, cudaStream_t stream) {
   // Partitions past ceil(len / tokens_per_split) are empty and weigh exactly
   // 0, so the merge reads only the live ones whenever lengths are known.
   m.lengths = a->lengths;
+  m.early_lengths = after_partition ? 1 : 0;
   m.num_heads = a->num_heads;
   m.tokens_per_split = a->tokens_per_split > 0 ? a->tokens_per_split : (1 << 30);
   m.rows = a->batch * a->num_heads;
@@ -476,7 +483,7 @@ extern "C" int pdl_merge(const PdlDecodeArgs *args, pdl_stream_t stream) {
   st = validate_workspace(args);
   if (st == PDL_OK) st = validate_out(args);
   if (st != PDL_OK) return st;
-  return run_merge(args, reinterpret_cast<cudaStream_t>(stream));
+  return run_merge(args, reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 extern "C" int pdl_lse_merge(const PdlMergeArgs *args, pdl_stream_t stream) {
@@ -643,7 +650,7 @@ extern "C" int pdl_paged_decode(const PdlDecodeArgs *args, pdl_stream_t stream) 
   const int mode = args->protocol == PDL_PROTOCOL_LSE ? MODE_LSE : MODE_MLA;
   st = run_partition(args, mode, s);
   if (st != PDL_OK) return st;
-  return run_merge(args, s);
+  return run_merge(args, s, true);
 }
 
 extern "C" int pdl_append_kv(const PdlAppendArgs *args, pdl_stream_t stream) {
@@ -778,5 +785,5 @@ extern "C" int pdl_paged_decode_static_scratch(const PdlDecodeArgs *args, pdl_st
   if (a.splits == 1 && (a.flags & PDL_FLAG_DIRECT_SINGLE)) return run_partition(&a, MODE_DIRECT, s);
   st = run_partition(&a, MODE_LSE, s);
   if (st != PDL_OK) return st;
-  return run_merge(&a, s);
+  return run_merge(&a, s, true);
 }

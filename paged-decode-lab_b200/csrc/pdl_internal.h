@@ -41,6 +41,7 @@ struct PartitionParams {
   int32_t mode;             // OutMode
   int32_t q_vec16;          // q rows 16-byte aligned (vector loads)
   int32_t write_empty;      // store -inf/0 for empty partitions
+  int32_t fill_splits;      // empty partitions (all heads of one row) per fill item
   __nv_bfloat16 *out;
   float *partial;
   float *lse;
@@ -49,6 +50,8 @@ struct PartitionParams {
   float *accums;
   uint32_t *fault;          // per-device fault word
   int32_t *sched;           // dynamic scheduling: [items claimed, finished CTAs], or null (static)
+  int32_t live;             // enumerate live items only (set by the launcher: multi-wave
+                            // launches of batches up to 512 rows)
 };
 
 // Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],
@@ -67,6 +70,8 @@ struct MergeParams {
   float *out_partial;       // FP32 [rows, D] merged partial, or null (LSE protocol)
   float *out_lse;           // FP32 [rows] merged LSE (-inf if empty), or null
   const int32_t *lengths;   // optional: bound the partitions read per row
+  int32_t early_lengths;    // launched right after the partition kernel: read lengths
+                            // before the dependency wait
   int32_t num_heads;
   int32_t tokens_per_split;
   int32_t rows;             // batch * num_heads

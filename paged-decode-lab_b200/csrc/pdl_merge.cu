@@ -40,14 +40,20 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   // The next decode step's partition kernel may be scheduled now; it waits
   // for this grid to complete before touching the workspace.
   allow_dependent_launch();
-  // Everything, the lengths included, is read after the partition kernel
-  // (and, through it, every kernel before it) has completed.
+  // The lengths are an input of the decode.  Launched right after this
+  // library's partition kernel (`early_lengths`), every kernel that may
+  // write them completed before that kernel let this one be scheduled (it
+  // triggers after its own dependency wait), so they are read before waiting
+  // for it; the workspace is always read after.
+  int len = 0;
+  if (p.early_lengths && p.lengths != nullptr && row < p.rows)
+    len = __ldg(p.lengths + row / p.num_heads);
   grid_dependency_wait();
   if (row >= p.rows) return;
   int live = p.splits;
   if (p.lengths != nullptr) {
-    const int len = max(__ldg(p.lengths + row / p.num_heads), 0);
-    live = min(live, (int)((len + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+    if (!p.early_lengths) len = __ldg(p.lengths + row / p.num_heads);
+    live = min(live, (int)((max(len, 0) + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
   }
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;

@@ -60,9 +60,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   static_assert(L::BYTES <= kTwoCtaSmemBytes, "two CTAs per SM");
   if (!smem_base_aligned(smem, p.fault)) return;
 
-  // The merge kernel that follows may be scheduled now; it waits for this
-  // grid to complete before reading the workspace.
-  allow_dependent_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -77,8 +74,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   // Launched with programmatic stream serialization: the set-up above may
   // overlap the previous kernel; its outputs (q, lengths, block table, the
   // workspace and scheduler words it may still read) are touched only after
-  // it has completed.
+  // it has completed.  Only then may the merge kernel that follows be
+  // scheduled: everything before this kernel has completed and is visible,
+  // so the merge can read the lengths before its own wait (it waits for this
+  // grid only to read the workspace).
   grid_dependency_wait();
+  allow_dependent_launch();
 
   if (warp == 0) {
     run_producer<D, T, NS>(&k_map, &v_map, p, kbuf, vbuf, full, empty, abort_flag, ring, lane);
@@ -271,8 +272,9 @@ cudaError_t launch_simt_t(const KernelLaunch &L, cudaStream_t stream) {
   }
   const int grid = min(L.params.n_items, blocks_per_sm[dev] * L.sm_count);
   if (grid <= 0) return cudaSuccess;
-  return launch_programmatic(kernel, dim3(grid), dim3(NTHREADS), smem, stream, *L.k_map,
-                             *L.v_map, L.params);
+  PartitionParams params = L.params;
+  params.live = live_schedule(params, grid);
+  return launch_programmatic(kernel, dim3(grid), dim3(NTHREADS), smem, stream, *L.k_map, *L.v_map, params);
 }
 
 template <int D>

@@ -4,6 +4,8 @@
 // consumer warps' softmax states into the stored outputs.
 #pragma once
 
+#include <climits>
+
 #include "pdl_device.cuh"
 
 namespace pdl {
@@ -59,178 +61,226 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
 }
 
 // ------------------------------------------------- the live-item schedule
-// Every CTA's producer warp derives the same schedule from the lengths (held
-// in registers: lane l owns rows l, l + 32, ...), so only work that exists is
-// ever handed out -- partitions past a row's length cost nothing -- and the
-// order is good for balance under dynamic scheduling, like longest-first:
-//   1. every FULL partition (tokens_per_split tokens), row-major;
+// Launches with more work items than CTAs (and batches of at most 32 * RMAX
+// rows) hand out only work that exists: every CTA's producer warp derives the
+// same schedule from the row lengths, so partitions past a row's length cost
+// no claim and no consumer round trip.  The order balances like
+// longest-first under dynamic scheduling:
+//   1. every FULL partition (tokens_per_split tokens), partition-major: every
+//      row's partition 0, then every row's partition 1, ...;
 //   2. every row's last, PARTIAL partition, in four size classes, largest
 //      first (in direct mode each row is one partial partition);
-//   3. one FILL item per row with empty partitions to store (or, in direct
-//      mode, per zero-length row).
-// Items 1 and 2 are expanded over the (KV head, sub-group) pairs, which vary
-// fastest, so concurrent CTAs read neighbouring bytes of the same pages.
+//   3. FILL items storing the empty partitions, in chunks of fill_splits
+//      partitions of all heads of one row (in direct mode, one per
+//      zero-length row), last, so idle CTAs take them.
+// Items of 1 and 2 are expanded over the (KV head, sub-group) pairs, which
+// vary fastest, so concurrent CTAs read neighbouring bytes of the same
+// pages.  Decoding an item of partition s costs a few warp ballots per
+// partition index up to s (partitions that every row has are decoded
+// directly), and no prefix sums, so a CTA's first item -- nearly always in
+// partition 0 -- is known right after the lengths arrive.  For a batch of
+// equal lengths the order is the dense partition-major one, which lets the
+// producer request the first item's block-table entries with the lengths.
+//
+// The code is kept small on purpose: the producer runs it once per item, so
+// it is rarely in the instruction cache, and rolled loops over the batch's
+// row chunks (the per-row arrays then live in L1-cached local memory) cost
+// far less than fully unrolled ones -- measured on B200, unrolling all 16
+// chunks added 4 to 40 us to short launches.
 constexpr int RMAX = 16;  // rows per lane: batches up to 512 rows use this schedule
 
 struct LiveSchedule {
   int len[RMAX];   // clamped length of row r * 32 + lane (0 past the batch)
-  int fpre[RMAX];  // exclusive row-major prefix of full partitions
-  int cls[RMAX];   // size class of the row's partial partition, -1 if none
-  int kpre[5];     // partial partitions of classes < c
-  int full;        // full partitions of the batch
-  int compute;     // compute items = (full + partial) * heads-and-sub-groups
-  int total;       // compute + fill items
+  int full[RMAX];  // its full partitions
+  int cls[RMAX];   // size class of its partial partition, -1 if none
+  int R;           // row chunks of the batch
 };
 
-__device__ __forceinline__ bool fill_row(const PartitionParams &p, int b, int len, int live) {
-  if (b >= p.batch) return false;
-  if (p.mode == MODE_DIRECT) return len == 0;
-  return p.write_empty && live < p.splits;
+// The launch parameters the schedule depends on (passed by value, so the
+// kernel's parameter block is not copied to local memory).
+struct SchedParams {
+  const int32_t *lengths;
+  int batch, heads, tps, splits, cap, direct, write_empty, fill_splits;
+};
+
+__device__ __forceinline__ SchedParams sched_params(const PartitionParams &p) {
+  SchedParams q;
+  q.lengths = p.lengths;
+  q.batch = p.batch;
+  q.heads = p.num_kv_heads * p.nsub;
+  q.tps = p.tokens_per_split;
+  q.splits = p.splits;
+  q.cap = row_capacity(p);
+  q.direct = p.mode == MODE_DIRECT;
+  q.write_empty = p.write_empty;
+  q.fill_splits = p.fill_splits;
+  return q;
 }
 
-__device__ __forceinline__ LiveSchedule build_schedule(const PartitionParams &p, int lane) {
-  LiveSchedule s;
-  const int tps = p.tokens_per_split;
-  const int R = (p.batch + 31) >> 5;
-  int maxlen = 0;
+// Fill chunks of row b.
+__device__ __forceinline__ int fill_chunks(const SchedParams &p, int b, int len, int live) {
+  if (b >= p.batch) return 0;
+  if (p.direct) return len == 0 ? 1 : 0;
+  if (!p.write_empty || live >= p.splits) return 0;
+  return (p.splits - live + p.fill_splits - 1) / p.fill_splits;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
-  for (int r = 0; r < RMAX; ++r) {
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);
+  return v;
+}
+
+static __device__ __noinline__ void build_schedule(const SchedParams p, int lane, LiveSchedule &s) {
+  const int tps = p.tps;
+  s.R = (p.batch + 31) >> 5;
+  int maxlen = 0;
+#pragma unroll 1
+  for (int r = 0; r < s.R; ++r) {
     const int b = r * 32 + lane;
-    s.len[r] = (r < R && b < p.batch) ? clamp_length(p, b) : 0;
+    s.len[r] = b < p.batch ? min(max(__ldg(p.lengths + b), 0), p.cap) : 0;
     maxlen = max(maxlen, s.len[r]);
   }
+  // Size classes are quarters of the longest possible partial partition:
+  // tokens_per_split, or in direct mode the longest row.
+  int span = tps;
+  if (p.direct) {
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) maxlen = max(maxlen, __shfl_xor_sync(FULL_MASK, maxlen, o));
-  // Size classes are quarters of the largest possible partial partition.
-  const int span = max(1, min(tps, maxlen));
+    for (int o = 16; o >= 1; o >>= 1) maxlen = max(maxlen, __shfl_xor_sync(FULL_MASK, maxlen, o));
+    span = max(1, maxlen);
+  }
+  const float inv_span = 4.f / (float)span;
+#pragma unroll 1
+  for (int r = 0; r < s.R; ++r) {
+    s.full[r] = s.len[r] / tps;
+    const int rem = s.len[r] - s.full[r] * tps;
+    s.cls[r] = rem > 0 ? min(3, (int)((float)(span - rem) * inv_span)) : -1;
+  }
+}
+
+// Items of the schedule: (full + partial partitions) * heads + fill chunks.
+static __device__ __noinline__ int schedule_total(const SchedParams p, const LiveSchedule &s,
+                                                  int lane) {
+  int parts = 0, fills = 0;
+#pragma unroll 1
+  for (int r = 0; r < s.R; ++r) {
+    const int live = s.full[r] + (s.cls[r] >= 0 ? 1 : 0);
+    parts += live;
+    fills += fill_chunks(p, r * 32 + lane, s.len[r], live);
+  }
+  return warp_sum(parts) * p.heads + warp_sum(fills);
+}
+
+// Item `item` of the schedule (every lane returns the same item); STOP past
+// the last one.  Partial partitions carry stop = the row's length.
+static __device__ __noinline__ WorkItem decode_live(const SchedParams p, const LiveSchedule &s,
+                                                    int item, int lane) {
+  WorkItem w = stop_item();
+  const int tps = p.tps;
+  const int heads = p.heads;
+  const int u = item / heads;
+  const int hs = item - u * heads;
+  int before = 0;  // row partitions of earlier groups
+  // 1. Full partitions, partition-major.  Partitions that every row has
+  // (below the smallest full count) are decoded directly.
+  int split = 0;
+  if (u >= p.batch) {
+    int fmin = INT_MAX;
+#pragma unroll 1
+    for (int r = 0; r < s.R; ++r)
+      if (r * 32 + lane < p.batch) fmin = min(fmin, s.full[r]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) fmin = min(fmin, __shfl_xor_sync(FULL_MASK, fmin, o));
+    if ((int64_t)u < (int64_t)p.batch * fmin) {
+      w.kind = ITEM_COMPUTE;
+      w.hs = hs;
+      w.b = u % p.batch;
+      w.split = u / p.batch;
+      w.start = w.split * tps;
+      w.stop = w.start + tps;
+      return w;
+    }
+    split = fmin;
+    before = p.batch * fmin;
+  }
+  // Group g < 0: full partitions of partition index `split`, one index after
+  // the other while any row has them; g = 0..3: partial partitions of size
+  // class g.  Rows of a group are taken in row order.
+  for (int g = -1; g < 4; ++g) {
+    int n_all;
+    do {
+      int k = u - before;
+      n_all = 0;
+#pragma unroll 1
+      for (int r = 0; r < s.R; ++r) {
+        const bool in = g < 0 ? s.full[r] > split : s.cls[r] == g;
+        const uint32_t m = __ballot_sync(FULL_MASK, in);
+        const int n = __popc(m);
+        if (k < n) {
+          const int src = nth_set_bit(m, k);
+          w.kind = ITEM_COMPUTE;
+          w.hs = hs;
+          w.b = r * 32 + src;
+          if (g < 0) {
+            w.split = split;
+            w.start = split * tps;
+            w.stop = w.start + tps;
+          } else {
+            const int len = __shfl_sync(FULL_MASK, s.len[r], src);
+            w.split = len / tps;
+            w.start = w.split * tps;
+            w.stop = len;
+          }
+          return w;
+        }
+        k -= n;
+        n_all += n;
+      }
+      before += n_all;
+      ++split;
+    } while (g < 0 && n_all > 0);
+  }
+  // 3. Fill chunks, row-major (a prefix sum over the rows' chunk counts).
+  const int j = item - before * heads;
   int carry = 0;
-#pragma unroll
-  for (int r = 0; r < RMAX; ++r) {
-    const int f = s.len[r] / tps;
-    const int rem = s.len[r] - f * tps;
-    int x = f;  // inclusive scan over the warp
+#pragma unroll 1
+  for (int r = 0; r < s.R; ++r) {
+    const int live = s.full[r] + (s.cls[r] >= 0 ? 1 : 0);
+    const int c = fill_chunks(p, r * 32 + lane, s.len[r], live);
+    int x = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(FULL_MASK, x, o);
       if (lane >= o) x += y;
     }
-    s.fpre[r] = carry + x - f;
+    const int pre = carry + x - c;
+    const uint32_t m = __ballot_sync(FULL_MASK, c > 0 && pre <= j && j < pre + c);
+    if (m) {
+      const int src = __ffs(m) - 1;
+      w.b = r * 32 + src;
+      const int first = __shfl_sync(FULL_MASK, live, src) +
+                        (j - __shfl_sync(FULL_MASK, pre, src)) * p.fill_splits;
+      w.kind = ITEM_FILL;
+      w.hs = -1;
+      w.split = first;
+      w.split_end = min(p.splits, first + p.fill_splits);
+      return w;
+    }
     carry += __shfl_sync(FULL_MASK, x, 31);
-    s.cls[r] = rem > 0 ? min(3, (int)(((int64_t)(span - rem) * 4) / span)) : -1;
-  }
-  s.full = carry;
-  s.kpre[0] = 0;
-  int fills = 0;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    int n = 0;
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r) n += __popc(__ballot_sync(FULL_MASK, s.cls[r] == c));
-    s.kpre[c + 1] = s.kpre[c] + n;
-  }
-#pragma unroll
-  for (int r = 0; r < RMAX; ++r) {
-    const int b = r * 32 + lane;
-    const int live = s.len[r] / tps + (s.cls[r] >= 0 ? 1 : 0);
-    fills += __popc(__ballot_sync(FULL_MASK, fill_row(p, b, s.len[r], live)));
-  }
-  const int heads = p.num_kv_heads * p.nsub;
-  s.compute = (s.full + s.kpre[4]) * heads;  // <= the host-checked dense item count
-  s.total = s.compute + fills;
-  return s;
-}
-
-// Item `item` (< s.total) of the schedule; every lane returns the same item.
-// COMPUTE items of a partial partition carry stop = the row's length.
-__device__ __forceinline__ WorkItem decode_live(const PartitionParams &p, const LiveSchedule &s, int item,
-                                int lane) {
-  WorkItem w = stop_item();
-  const int tps = p.tokens_per_split;
-  if (item < s.compute) {
-    const int heads = p.num_kv_heads * p.nsub;
-    const int u = item / heads;
-    w.kind = ITEM_COMPUTE;
-    w.hs = item - u * heads;
-    if (u < s.full) {
-      // The row whose full partitions [fpre, fpre + f) hold u.  (Values of
-      // the matching row are read inside the unrolled loops: an array
-      // indexed by a run-time chunk would move to local memory.)
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        int next = __shfl_down_sync(FULL_MASK, s.fpre[r], 1);
-        const int head_next = __shfl_sync(FULL_MASK, s.fpre[r + 1 < RMAX ? r + 1 : r], 0);
-        if (lane == 31) next = r + 1 < RMAX ? head_next : s.full;
-        const uint32_t m = __ballot_sync(FULL_MASK, s.fpre[r] <= u && u < next);
-        if (m) {
-          const int src = __ffs(m) - 1;
-          w.b = r * 32 + src;
-          w.split = u - __shfl_sync(FULL_MASK, s.fpre[r], src);
-        }
-      }
-      w.start = w.split * tps;
-      w.stop = w.start + tps;
-    } else {
-      int k = u - s.full, c = 0, first = 0;
-#pragma unroll
-      for (int j = 1; j < 4; ++j) {
-        if (k >= s.kpre[j]) {
-          c = j;
-          first = s.kpre[j];
-        }
-      }
-      k -= first;
-      bool found = false;
-      int len = 0;
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        const uint32_t m = __ballot_sync(FULL_MASK, s.cls[r] == c);
-        const int n = __popc(m);
-        if (!found && k < n) {
-          const int src = nth_set_bit(m, k);
-          w.b = r * 32 + src;
-          len = __shfl_sync(FULL_MASK, s.len[r], src);
-          found = true;
-        } else if (!found) {
-          k -= n;
-        }
-      }
-      w.split = len / tps;
-      w.start = w.split * tps;
-      w.stop = len;
-    }
-  } else {
-    int k = item - s.compute;
-    bool found = false;
-    int len = 0;
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
-      const int b = r * 32 + lane;
-      const int live = s.len[r] / tps + (s.cls[r] >= 0 ? 1 : 0);
-      const uint32_t m = __ballot_sync(FULL_MASK, fill_row(p, b, s.len[r], live));
-      const int n = __popc(m);
-      if (!found && k < n) {
-        const int src = nth_set_bit(m, k);
-        w.b = r * 32 + src;
-        len = __shfl_sync(FULL_MASK, s.len[r], src);
-        found = true;
-      } else if (!found) {
-        k -= n;
-      }
-    }
-    w.kind = ITEM_FILL;
-    w.hs = -1;
-    w.split = (int)(((int64_t)len + tps - 1) / tps);
-    w.split_end = p.splits;
   }
   return w;
 }
 
-// Batches above 32 * RMAX rows enumerate every (row, KV head, sub-group,
-// partition) instead; empty ones become single-partition FILL items (or are
-// skipped when empty partitions are not stored).
+// Single-wave launches (at most one item per CTA) and batches above
+// 32 * RMAX rows enumerate every (row, KV head, sub-group, partition)
+// instead; empty ones become single-partition FILL items (or are skipped
+// when empty partitions are not stored).  The row length and the first 32
+// block-table entries of the partition are requested together, so an item,
+// and its first pages, are known after one round trip.
 //   static:  item = ((b * num_kv_heads + kvh) * nsub + sub) * splits + split
 //   dynamic: item = split * (batch * num_kv_heads * nsub) + group
-__device__ __forceinline__ WorkItem decode_dense(const PartitionParams &p, int item, bool dynamic, bool &skip) {
+__device__ __forceinline__ WorkItem decode_dense(const PartitionParams &p, int item, bool dynamic,
+                                                 int lane, bool &skip, int &base, int &my_page) {
   WorkItem w = stop_item();
   const int per_row = p.num_kv_heads * p.nsub;
   int rest;
@@ -244,8 +294,11 @@ __device__ __forceinline__ WorkItem decode_dense(const PartitionParams &p, int i
   }
   w.b = rest / per_row;
   w.hs = rest % per_row;
-  const int len = clamp_length(p, w.b);
   const int64_t start = (int64_t)w.split * p.tokens_per_split;
+  base = start < (int64_t)row_capacity(p) ? (int)(start >> 8) : -64;
+  my_page = (base >= 0 && base + lane < p.table_width)
+                ? __ldg(p.table + (int64_t)w.b * p.table_stride + base + lane) : 0;
+  const int len = clamp_length(p, w.b);
   const int64_t stop = min((int64_t)len, start + p.tokens_per_split);
   skip = false;
   if (start < stop) {
@@ -343,8 +396,8 @@ __device__ __forceinline__ WorkItem consumer_next(const ItemRing &r, uint32_t &k
 // for compute items, reads the partition's block-table entries (32 per load,
 // one per lane, never past the table width) and issues one T-token tile of K
 // and V per stage as D/64 TMA boxes each.  T divides 256, so a tile never
-// spans two pages.  The next item is claimed before this one's copies are
-// issued, so the atomic's round trip overlaps them.
+// spans two pages.  The next item is claimed once this one's first copies
+// are issued, so the atomic's round trip overlaps them.
 template <int D, int T, int NS>
 __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
                              const PartitionParams &p, uint8_t *kbuf, uint8_t *vbuf,
@@ -358,36 +411,74 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
     prefetch_tensormap(k_map);
     prefetch_tensormap(v_map);
   }
-  const bool live = p.batch <= 32 * RMAX;
-  LiveSchedule sched;
-  int total = p.n_items;
-  if (live) {
-    sched = build_schedule(p, lane);
-    total = sched.total;
-  }
-  const bool dynamic = p.sched != nullptr && total > (int)gridDim.x;
-  uint32_t it = 0, k = 0;
-  bool ok = true;
+  // The live schedule serves launches with more items than CTAs (set by the
+  // launcher); a single wave is enumerated densely (decode_dense).
+  const bool live = p.live != 0;
+  const int heads = p.num_kv_heads * p.nsub;
   int item = blockIdx.x;
+  const SchedParams sp = sched_params(p);
+  LiveSchedule sched;
+  // Live schedule: the first item's block-table entries are requested before
+  // the lengths arrive, for the dense partition-major guess (row u % batch,
+  // partition u / batch with u = item / heads), which the live order equals
+  // when every row has the same length.
+  int guess_row = -1, guess_base = -1, guess_page = 0;
+  if (live) {
+    const int u0 = item / heads;
+    guess_row = u0 % p.batch;
+    const int64_t first_tok = (int64_t)(u0 / p.batch) * p.tokens_per_split;
+    guess_base = first_tok < (int64_t)row_capacity(p) ? (int)(first_tok >> 8) : -1;
+    if (guess_base >= 0 && guess_base + lane < p.table_width)
+      guess_page = __ldg(p.table + (int64_t)guess_row * p.table_stride + guess_base + lane);
+    build_schedule(sp, lane, sched);
+  }
+  // Items of this launch: known at once when dense; for the live schedule
+  // computed once the first item's copies are issued.
+  int total = live ? -1 : p.n_items;
+  int dynamic = -1;  // decided at the first claim: is there an item past the first wave?
+  uint32_t it = 0, k = 0;
+  bool ok = true, first = true;
   while (ok) {
-    if (item >= total) {
-      publish(ring, k, stop_item(), p.fault, abort_flag, lane);
+    bool skip = false;
+    int base = -64, my_page = 0;
+    WorkItem w = stop_item();
+    if (total < 0 || item < total) {
+      if (live) {
+        w = decode_live(sp, sched, item, lane);
+        if (w.kind == ITEM_COMPUTE) {
+          base = w.start >> 8;
+          if (first && w.b == guess_row && base == guess_base)
+            my_page = guess_page;
+          else
+            my_page = base + lane < p.table_width
+                          ? __ldg(p.table + (int64_t)w.b * p.table_stride + base + lane) : 0;
+        }
+      } else {
+        w = decode_dense(p, item, p.sched != nullptr, lane, skip, base, my_page);
+      }
+    }
+    if (w.kind == ITEM_STOP) {
+      publish(ring, k, w, p.fault, abort_flag, lane);
       break;
     }
-    bool skip = false;
-    const WorkItem w = live ? decode_live(p, sched, item, lane) : decode_dense(p, item, dynamic, skip);
-    // Claim the next item now; its value is needed only after the copies.
-    int claimed = 0;
-    if (dynamic && lane == 0) claimed = atomicAdd(p.sched, 1);
     if (!skip && !publish(ring, k, w, p.fault, abort_flag, lane)) {
       ok = false;
       break;
     }
+    // The next item is claimed once this one's first copies are issued, so
+    // the atomic's round trip (and the live schedule's total) overlaps them.
+    int claimed = 0;
+    bool claimed_yet = false;
+    auto claim = [&]() {
+      if (claimed_yet) return;
+      claimed_yet = true;
+      if (total < 0) total = schedule_total(sp, sched, lane);
+      if (dynamic < 0) dynamic = p.sched != nullptr && total > (int)gridDim.x;
+      if (dynamic && lane == 0) claimed = atomicAdd(p.sched, 1);
+    };
     if (w.kind == ITEM_COMPUTE) {
       const int32_t *trow = p.table + (int64_t)w.b * p.table_stride;
       const int kvh = w.hs / p.nsub;
-      int base = w.start >> 8;
-      int my_page = base + lane < p.table_width ? __ldg(trow + base + lane) : 0;
       const int t0 = w.start / T * T;
       const int ntiles = (w.stop - t0 + T - 1) / T;
       for (int i = 0; i < ntiles; ++i, ++it) {
@@ -416,20 +507,26 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
         }
         ok = __shfl_sync(FULL_MASK, ok, 0);
         if (!ok) break;
+        if (i + 1 == min(ntiles, NS)) claim();
       }
     }
+    first = false;
+    if (!ok) break;
+    claim();
     item = dynamic ? (int)gridDim.x + __shfl_sync(FULL_MASK, claimed, 0) : item + (int)gridDim.x;
   }
   if (!ok && lane == 0) {
     // Let the copies already issued land before the CTA exits.
-    const uint32_t first = it > NS ? it - NS : 0;
-    for (uint32_t j = first; j < it; ++j)
+    const uint32_t j0 = it > NS ? it - NS : 0;
+    for (uint32_t j = j0; j < it; ++j)
       mbar_wait_bounded(&full[j % NS], (j / NS) & 1, p.fault, FAULT_DRAIN_WAIT);
   }
   // Count this CTA as finished; the last one resets the scheduler words for
   // the next launch (every CTA's final claim precedes its count, and no
-  // claim follows the last count).  Every CTA computed the same `dynamic`.
-  if (dynamic && lane == 0) {
+  // claim follows the last count).  Every CTA that claimed computed the same
+  // `dynamic` (a CTA whose first item was past the end never claims, and
+  // then the first wave held every item, so no CTA used the counter).
+  if (dynamic > 0 && lane == 0) {
     __threadfence();
     if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
       atomicExch(p.sched, 0);
@@ -534,6 +631,13 @@ __device__ void combine_and_store(const PartitionParams &p, const WorkItem &w, i
       }
     }
   }
+}
+
+// Host: the live schedule pays when a launch has more (dense) items than CTAs
+// -- partitions past the rows' lengths would otherwise cost claims -- and the
+// lengths fit the producer's registers and local memory.
+inline int live_schedule(const PartitionParams &p, int grid) {
+  return p.batch <= 32 * RMAX && p.n_items > grid ? 1 : 0;
 }
 
 // Dynamic shared memory one CTA may use so that two CTAs share an SM

@@ -166,12 +166,16 @@ def test_split_layout_invariance(kernel):
 @pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("protocol", ["lse", "mla"])
 @pytest.mark.parametrize("flags", [0, "dynamic", "skip", "dynamic+skip"])
-def test_every_partition_slot_follows_the_workspace_contract(kernel, protocol, flags):
+@pytest.mark.parametrize("hq,hkv,d,tps,splits", [(8, 2, 128, 512, 8), (16, 4, 256, 128, 33)])
+def test_every_partition_slot_follows_the_workspace_contract(kernel, protocol, flags, hq, hkv,
+                                                            d, tps, splits):
     """Live partitions hold the oracle's values; empty ones are stored as empty
     (partial 0 / LSE -inf, or (-inf, 0, 0)) unless PDL_FLAG_SKIP_EMPTY, which
-    leaves them untouched.  The workspace starts NaN-poisoned."""
+    leaves them untouched.  The workspace starts NaN-poisoned.  The first
+    geometry runs several work items per CTA (the live schedule) and stores
+    several empty partitions per fill item, the second one per item."""
     lengths = [3000, 0, 1, 4096, 257, 2048, 2049, 0]
-    rows, hq, hkv, d, tps, splits = len(lengths), 8, 2, 128, 512, 8
+    rows = len(lengths)
     case = cases.make_case(lengths, hq, hkv, d, seed=12, capacity=4096)
     q, k, v, table, lens = device_case(case)
     bits = {"dynamic": ops.FLAG_DYNAMIC, "skip": ops.FLAG_SKIP_EMPTY,
