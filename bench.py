@@ -1,21 +1,25 @@
 """Benchmark of the paged decode-attention operator (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4] [--impl ours|reference]
 
 A step is one decode call (partition + LSE merge) over one batch of the chosen
-BASELINE config with inputs resident in HBM.  Default workload: config 2 (MHA
-D=64, B=64, Hq=Hkv=32, 2048 tokens per row, 1024-token split-K partitions),
-the single-GPU config the metric is quoted on.
+BASELINE config with inputs resident in HBM.  Default workload: config 4, the
+largest config stated for one GPU -- variable-length serving batch, B=128,
+Hq=32, Hkv=8, D=128, lognormal lengths (median 4096, clipped to [1, 32768],
+every 32nd row 0; 3.07 GB of KV per step) -- split with this library's B200
+plan (8 partitions of 4096 tokens, dynamic scheduling).
 
 * ``value``: KV GB/s = algorithmic KV bytes / device time.  K steps are
   captured in one CUDA graph; that K-step window is replayed R times back to
   back (R sized to about half a second so the clock sampler sees it) between
   CUDA events, max over ranks.  When a config's KV pool is smaller than 2x L2,
   steps rotate over independent input copies so every step reads HBM.
-* ``e2e``: the same metric through the public API (``matched_decode``) with
-  host buffers: each step copies q / block table / lengths from one pinned
-  host staging buffer (one H2D copy), decodes and copies the output back.
-  The KV cache is resident device state, as in serving.
+* ``convergence``: the same step captured as 32- and 128-step graphs;
+  |t32 - t128| / t128 (required <= 0.05).
+* ``e2e``: the same metric through the public API (``matched_decode``, or
+  ``ContextParallelDecode``) with host buffers: each step copies q / block
+  table / lengths from pinned host memory and the output back, inside the
+  timed region.  The KV cache is resident device state, as in serving.
 * ``roofline``: the partition kernel alone (K launches per graph window) vs
   the measured HBM copy bandwidth in MEASURED_PEAKS.json; ``traffic`` is the
   per-launch DRAM bytes of the ncu summary committed under profiles/.
@@ -23,11 +27,22 @@ the single-GPU config the metric is quoted on.
   bounded sample of the same workload on the host cores (rank 0, N = 1).
 * ``--impl reference``: that CPU implementation alone, on all host cores.
 
-Multi-GPU (torchrun): every rank decodes its own independent batch (batch
-sharding, no collective on the data path); ``value`` = all ranks' bytes / the
-slowest rank's time ("scaling": "weak").
+Multi-GPU (torchrun), ``--mode``:
+  head     (default) one global batch, KV heads split over the ranks, no
+           collective on the data path ("scaling": "strong");
+  batch    one global batch, rows split token-balanced over the ranks
+           ("strong");
+  context  one global batch, each row's pages split over the ranks, one
+           exchange of (partial, LSE) per step (default for cfg5; "strong");
+  replica  every rank decodes its own batch ("weak").
+``value`` = the global batch's KV bytes (every rank's for replica) / the
+slowest rank's time.  Before timing, the ranks' outputs are gathered and
+compared with a one-GPU decode of the global batch on rank 0: bit-exact for
+head and batch sharding (same partition bounds), within 2^-7 for context
+parallelism (other partition bounds); the line carries ``parity``.
 """
 import argparse
+import copy
 import datetime
 import json
 import math
@@ -46,22 +61,24 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn achieved KV HBM GB/s"
 UNIT = "GB/s"
 L2_BYTES = 126e6
+CONVERGENCE_LIMIT = 0.05
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", default="cfg2", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"))
+    ap.add_argument("--config", default="cfg4", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"))
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--context", type=int, default=None)
     ap.add_argument("--splits", type=int, default=None, help="matched plan split count")
     ap.add_argument("--kernel", default="auto", choices=("auto", "simt", "mma"))
-    ap.add_argument("--mode", default="batch", choices=("batch", "context", "head"),
-                    help="N>1: independent batch per rank (weak), one batch split by context "
-                         "across ranks (strong), or one batch split by KV head (strong)")
+    ap.add_argument("--mode", default="auto", choices=("auto", "head", "batch", "context", "replica"),
+                    help="N>1: split one batch by KV head, by rows or by context (strong "
+                         "scaling), or run an independent batch per rank (weak); auto = context "
+                         "for cfg5, else head")
     ap.add_argument("--exchange", default="p2p", choices=("nccl", "p2p"),
                     help="context mode: NCCL all-gather between two merge kernels, or one "
                          "kernel storing into peers' buffers over NVLink (pdl_exchange_merge)")
@@ -75,6 +92,7 @@ def parse_args():
     ap.add_argument("--window-seconds", type=float, default=0.5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the N>1 parity check")
     ap.add_argument("--sweep", action="store_true",
                     help="partition-kernel GB/s for every (head_dim, group, kernel) at ~1 GB of "
                          "KV (one JSON line per point; not the contract line)")
@@ -82,7 +100,16 @@ def parse_args():
                     help="under torchrun (N>1): time the context-parallel combine alone, NCCL "
                          "path (local merge, all-gather, merge) vs the peer-memory exchange "
                          "kernel (one JSON line per shape; not the contract line)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
+
+
+def resolve_mode(args, world):
+    """The multi-GPU mode of this run ("single" on one GPU)."""
+    if world == 1:
+        return "single"
+    if args.mode != "auto":
+        return args.mode
+    return "context" if args.config == "cfg5" else "head"
 
 
 def sweep(reps=20):
@@ -159,6 +186,17 @@ def cpu_sample_cap(name):
     return 65536 if name == "cfg5" else None
 
 
+def blas_info():
+    """The BLAS library NumPy uses (the CPU baseline's matrix products)."""
+    try:
+        import numpy as np
+        deps = np.show_config(mode="dicts").get("Build Dependencies", {})
+        blas = deps.get("blas", {})
+        return f"{blas.get('name', 'unknown')} {blas.get('version', '')}".strip()
+    except Exception as exc:  # depends on how NumPy was built
+        return f"unknown ({type(exc).__name__})"
+
+
 def run_cpu(name, steps, warmup, seconds=None):
     """Time the oracle port on host cores; returns (GB/s, cores, sample, s/pass, passes)."""
     from oracle import cpu_runner
@@ -181,6 +219,13 @@ def run_cpu(name, steps, warmup, seconds=None):
     finally:
         runner.close()
         cpu_runner.release()
+
+
+def cpu_line(gbs, cores, desc):
+    """The cpu_baseline object: the oracle port on `cores` single-threaded BLAS workers."""
+    return {"value": round(gbs, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": desc, "blas": blas_info(), "blas_threads_per_worker": 1,
+            "workers": cores}
 
 
 # ---------------------------------------------------------------- clocks
@@ -225,7 +270,7 @@ class ClockSampler:
     def summary(self, windows):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons, n = [], None, set(), 0
+        sm, mx, reasons = [], None, set()
         for t, line in self.samples:
             if not any(t0 - 0.05 <= t <= t1 + 0.15 for t0, t1 in windows):
                 continue
@@ -243,6 +288,32 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def gpu_sharing(index):
+    """Read-only check for other processes computing on this GPU (nvidia-smi).
+
+    Returns {"gpu_shared": bool or None, "foreign_compute_apps": n or None};
+    None when the query is unavailable (no nvidia-smi, or a PID namespace
+    hides the processes).
+    """
+    try:
+        uuid = subprocess.run(["nvidia-smi", f"--id={index}", "--query-gpu=uuid",
+                               "--format=csv,noheader"], capture_output=True, text=True,
+                              timeout=20).stdout.strip()
+        apps = subprocess.run(["nvidia-smi", "--query-compute-apps=pid,gpu_uuid",
+                               "--format=csv,noheader"], capture_output=True, text=True,
+                              timeout=20)
+    except (OSError, subprocess.SubprocessError):
+        return {"gpu_shared": None, "foreign_compute_apps": None}
+    if apps.returncode != 0 or not uuid:
+        return {"gpu_shared": None, "foreign_compute_apps": None}
+    mine, foreign = os.getpid(), 0
+    for line in apps.stdout.splitlines():
+        parts = [p.strip() for p in line.split(",")]
+        if len(parts) >= 2 and parts[1] == uuid and parts[0].isdigit() and int(parts[0]) != mine:
+            foreign += 1
+    return {"gpu_shared": foreign > 0, "foreign_compute_apps": foreign}
+
+
 # ---------------------------------------------------------------- helpers
 def measured_peak():
     path = ROOT / "MEASURED_PEAKS.json"
@@ -258,7 +329,7 @@ def committed_traffic(workload, kernel):
         m = re.search(rf"^traffic\[{re.escape(workload)}\]\[{re.escape(kernel)}\]:\s*(\d+)",
                       path.read_text(), re.M)
         if m:
-            return int(m.group(1)), path.name
+            return int(m.group(1)), f"committed ncu summary profiles/{path.name}"
     return None, None
 
 
@@ -270,8 +341,7 @@ def reference_line(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-valued inputs)",
             "data": "synthetic (seeded, NumPy)",
             "config": {"workload": args.config, "sample": desc},
-            "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": cores,
-                             "kind": "port", "sample": desc},
+            "cpu_baseline": cpu_line(gbs, cores, desc),
             "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -357,8 +427,73 @@ def exchange_micro(reps=20, steps=20):
     dist.destroy_process_group()
 
 
-def main():
-    args = parse_args()
+# ---------------------------------------------------------------- multi-GPU parity
+def full_decode(w, tokens_per_split, splits, kernel, device):
+    """One-GPU decode of a whole batch with the given partition size: the
+    parity reference of the sharded modes (same kernels and bounds per row)."""
+    import torch
+    from paged_decode import ops
+    b, hq, d = w.q.shape
+    out = torch.empty(b, hq, d, dtype=torch.bfloat16, device=device)
+    partial = torch.empty(b, hq, splits, d, device=device)
+    lse = torch.empty(b, hq, splits, device=device)
+    ops.paged_decode(ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
+                                     tokens_per_split=tokens_per_split, splits=splits,
+                                     protocol=ops.PROTOCOL_LSE, kernel=kernel, out=out,
+                                     partial=partial, lse=lse), device)
+    torch.cuda.synchronize(device)
+    return out
+
+
+def check_parity(mode, out, full, plan, shards, kernel, world, rank, device):
+    """Gather every rank's output and compare it on rank 0 with a one-GPU
+    decode of the global batch; every rank takes the same collective steps."""
+    import torch
+    import torch.distributed as dist
+    ok, err = True, 0.0
+    if mode == "context":
+        if rank == 0:
+            from paged_decode import ops
+            from paged_decode.splitkv_plan import make_b200_plan
+            g = make_b200_plan(full.spec, ops.sm_count(device))
+            want = full_decode(full, g.tokens_per_split, g.splits, kernel, device)
+            err = float((out.float() - want.float()).abs().max().item())
+            ok = err <= 2.0 ** -7 and bool(torch.isfinite(out.float()).all().item())
+        reference = "one-GPU decode of the global batch (B200 plan), max-abs 2^-7"
+    elif mode == "head":
+        gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=device)
+        dist.all_gather_into_tensor(gathered, out.contiguous())
+        if rank == 0:
+            got = torch.cat(list(gathered), dim=1)
+            want = full_decode(full, plan.tokens_per_split, plan.splits, kernel, device)
+            ok = torch.equal(got, want)
+            err = float((got.float() - want.float()).abs().max().item())
+        reference = "one-GPU decode of the global batch, same partitions: bit-exact"
+    elif mode == "batch":
+        most = max(len(s) for s in shards)
+        pad = torch.zeros((most,) + tuple(out.shape[1:]), dtype=out.dtype, device=device)
+        pad[:out.shape[0]] = out
+        gathered = torch.empty((world, most) + tuple(out.shape[1:]), dtype=out.dtype,
+                               device=device)
+        dist.all_gather_into_tensor(gathered, pad)
+        if rank == 0:
+            got = torch.empty_like(full.q)
+            for r, rows in enumerate(shards):
+                got[torch.as_tensor(rows, device=device)] = gathered[r, :len(rows)]
+            want = full_decode(full, plan.tokens_per_split, plan.splits, kernel, device)
+            ok = torch.equal(got, want)
+            err = float((got.float() - want.float()).abs().max().item())
+        reference = "one-GPU decode of the global batch, same partitions: bit-exact"
+    else:  # replica: independent batches, nothing to gather
+        return {"mode": mode, "ok": True, "reference": "none (independent batches)"}
+    flag = torch.tensor([1 if ok else 0], device=device)
+    dist.broadcast(flag, 0)
+    return {"mode": mode, "ok": bool(flag.item()), "max_abs_err": err, "reference": reference}
+
+
+# ---------------------------------------------------------------- main
+def main(argv=None):
+    args = parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -377,17 +512,21 @@ def main():
         exchange_micro()
         return 0
 
+    mode = resolve_mode(args, world)
+    if args.append and mode == "context":
+        raise SystemExit("--append is not supported with --mode context")
+
     # CPU baseline first (rank 0, N = 1): its spawn pool starts before any CUDA work.
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, cores, desc, per_pass, n = run_cpu(args.config, 1, 1, seconds=args.cpu_seconds)
-        cpu = {"value": round(gbs, 4), "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{desc}; {n} passes, {per_pass * 1e3:.1f} ms each"}
+        cpu = cpu_line(gbs, cores, f"{desc}; {n} passes, {per_pass * 1e3:.1f} ms each")
 
     import torch
     import torch.distributed as dist
-    from paged_decode import ops
+    from paged_decode import ops, parallel
     from paged_decode.matched_splitkv import allocate_matched_resources, matched_decode
+    from paged_decode.spec import DecodeSpec
     from paged_decode.workloads import make_workload
 
     if world > 1:
@@ -396,8 +535,10 @@ def main():
                                 device_id=torch.device("cuda", local))
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
+    sharing = gpu_sharing(device.index)
     clocks = ClockSampler(device.index).start()
     windows = []
+    sms = ops.sm_count(device)
 
     def max_over_ranks(x):
         if world == 1:
@@ -406,71 +547,85 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    context = args.mode == "context" and world > 1
-    heads = args.mode == "head" and world > 1
-    if args.append and context:
-        raise SystemExit("--append is not supported with --mode context")
-    strong = context or heads
-
-    def build(seed=0):
-        """This rank's workload: its own batch (batch mode), or the global batch
-        (same seed on every rank) cut to this rank's KV heads (head mode) or,
-        later, to its page range (context mode)."""
-        w = make_workload(args.config, device=device, batch=args.batch, context=args.context,
-                          rank=0 if strong else rank, seed=seed)
-        if heads:
-            from paged_decode import parallel
-            from paged_decode.spec import DecodeSpec
-            sp = w.spec
-            w.q, w.k, w.v = parallel.shard_head_pool(w.k, w.v, w.q, rank, world,
-                                                     sp.num_heads, sp.num_kv_heads)
-            w.spec = DecodeSpec(sp.max_batch, sp.num_heads // world, sp.num_kv_heads // world,
-                                sp.head_dim, sp.max_context_len)
-            torch.cuda.empty_cache()
-        return w
-
-    first = build()
-    # Job bytes: the global batch's KV bytes (strong modes) or every rank's own.
-    kv_bytes = first.kv_bytes * (world if heads else 1)
+    strong = mode in ("head", "batch", "context")
     stream = torch.cuda.current_stream(device)
     K = args.steps
-    if context:
-        from paged_decode import parallel
-        k_loc, v_loc, t_loc = parallel.shard_context_pool(first.k, first.v, first.table, rank,
-                                                          world)
-        first.k, first.v, first.table = k_loc, v_loc, t_loc
+    seed_rank = rank if mode == "replica" else 0
+
+    # ---- this rank's work --------------------------------------------------
+    glob = make_workload(args.config, device=device, batch=args.batch, context=args.context,
+                         rank=seed_rank)
+    gspec = glob.spec
+    job_bytes = glob.kv_bytes * (world if mode == "replica" else 1)
+    shards = None
+    if mode == "batch":
+        shards = parallel.batch_shards(glob.lengths.cpu().tolist(), world)
+        if not all(shards):
+            raise SystemExit("batch mode needs at least one row per rank")
+    # Rank 0 keeps the global batch for the parity check (a shallow copy: the
+    # tensors survive when the workload below is cut to this rank's share).
+    full = copy.copy(glob) if world > 1 and rank == 0 and not args.no_parity else None
+
+    def local_workload(seed):
+        """This rank's tensors for input copy `seed` (copy 0 is the global batch)."""
+        w = glob if seed == 0 else make_workload(args.config, device=device, batch=args.batch,
+                                                 context=args.context, rank=seed_rank, seed=seed)
+        if mode == "head":
+            w.q, w.k, w.v = parallel.shard_head_pool(w.k, w.v, w.q, rank, world,
+                                                     gspec.num_heads, gspec.num_kv_heads)
+            w.spec = DecodeSpec(gspec.max_batch, gspec.num_heads // world,
+                                gspec.num_kv_heads // world, gspec.head_dim,
+                                gspec.max_context_len)
+        elif mode == "batch":
+            rows = shards[rank]
+            w.k, w.v, w.table, w.lengths = parallel.shard_batch_pool(w.k, w.v, w.table,
+                                                                     w.lengths, rows)
+            w.q = w.q[torch.as_tensor(rows, device=device)].contiguous()
+            w.spec = DecodeSpec(len(rows), gspec.num_heads, gspec.num_kv_heads, gspec.head_dim,
+                                gspec.max_context_len)
+        return w
+
+    cp = None
+    if mode == "context":
+        w0 = copy.copy(glob)
+        w0.k, w0.v, w0.table = parallel.shard_context_pool(glob.k, glob.v, glob.table, rank,
+                                                           world)
+        glob = None
         torch.cuda.empty_cache()
-        cp = parallel.ContextParallelDecode(first.spec, device, kernel=args.kernel,
+        cp = parallel.ContextParallelDecode(gspec, device, kernel=args.kernel,
                                             local_splits=args.splits or 0,
                                             exchange=args.exchange)
-        copies, wls = 1, [first]
-        cp(first.q, k_loc, v_loc, t_loc, first.lengths)
+        cp(w0.q, w0.k, w0.v, w0.table, w0.lengths)
         plan = cp.plan
-        local_bytes = int(cp.local_len.sum().item()) * first.spec.num_kv_heads * \
-            first.spec.head_dim * 4
+        local_bytes = int(cp.local_len.to(torch.int64).sum().item()) * gspec.num_kv_heads * \
+            gspec.head_dim * 4
+        copies, wls, out_slots = 1, [w0], None
 
         def decode_call(w, slot=0):
             return cp(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale)
 
-        out_slots = None  # one output buffer: copied out per step (below)
-
-        part_args = [cp._launch_args(first.q, k_loc, v_loc, t_loc, first.scale)[0]]
+        part_args = [cp._launch_args(w0.q, w0.k, w0.v, w0.table, w0.scale)[0]]
         out_buf = cp.out
     else:
-        pool_bytes = first.k.numel() * 2 * 2
+        w0 = local_workload(0)
+        pool_bytes = w0.k.numel() * 2 * 2
         copies = 1 if (pool_bytes >= 2 * L2_BYTES or args.hot) else \
             min(64, math.ceil(2 * L2_BYTES / pool_bytes))
-        wls = [first] + [build(seed=c) for c in range(1, copies)]
-        res = allocate_matched_resources(
-            first.spec, device,
-            plan=config_plan(args.config, args, first.spec, ops.sm_count(device)))
-        plan = res.plan
-        local_bytes = first.kv_bytes
-
+        wls = [w0] + [local_workload(c) for c in range(1, copies)]
+        if mode == "batch":
+            # One partition size on every rank (the plan of the largest shard),
+            # so each row's bounds equal the one-GPU decode's.
+            most = max(len(s) for s in shards)
+            plan = config_plan(args.config, args, DecodeSpec(most, gspec.num_heads,
+                                                             gspec.num_kv_heads, gspec.head_dim,
+                                                             gspec.max_context_len), sms)
+        else:
+            plan = config_plan(args.config, args, w0.spec, sms)
+        res = allocate_matched_resources(w0.spec, device, plan=plan)
+        local_bytes = w0.kv_bytes
         # A second resource set lets step i+1 compute while step i's output
         # is still being copied to the host.
-        out_slots = [res, allocate_matched_resources(first.spec, device, plan=plan)]
-
+        out_slots = [res, allocate_matched_resources(w0.spec, device, plan=plan)]
         if args.append:
             from paged_decode.kvcache import append_decode_kv
             for w in wls:
@@ -506,7 +661,17 @@ def main():
         partition_only(i)
     torch.cuda.synchronize(device)
 
-    def capture(fn):
+    # ---- multi-GPU parity: every rank's output against one GPU --------------
+    parity = None
+    if world > 1 and not args.no_parity and not args.append:
+        out = decode_call(wls[0]).clone()
+        torch.cuda.synchronize(device)
+        parity = check_parity(mode, out, full, plan, shards, args.kernel, world, rank, device)
+        del out
+    full = None
+    torch.cuda.empty_cache()
+
+    def capture(fn, n):
         side = torch.cuda.Stream(device)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
@@ -514,14 +679,14 @@ def main():
         stream.wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            for i in range(K):
+            for i in range(n):
                 fn(i)
         graph.replay()
         torch.cuda.synchronize(device)
         return graph
 
-    def timed(graph, seconds):
-        """Replay the K-step graph in back-to-back windows; returns (total ms, windows)."""
+    def timed(graph, seconds, record=True):
+        """Replay a graph in back-to-back windows; returns (ms, max over ranks; replays)."""
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         graph.replay()
@@ -538,24 +703,39 @@ def main():
             graph.replay()
         e1.record(stream)
         torch.cuda.synchronize(device)
-        windows.append((t0, time.monotonic()))
+        if record:
+            windows.append((t0, time.monotonic()))
         return max_over_ranks(e0.elapsed_time(e1)), reps
 
-    step_graph = capture(step)
+    step_graph = capture(step, K)
     total_ms, reps = timed(step_graph, args.window_seconds)
+    del step_graph
     ms_per_step = total_ms / (reps * K)
-    job_bytes = kv_bytes if strong else world * kv_bytes
     value = job_bytes / (ms_per_step / 1e3) / 1e9
 
-    part_graph = capture(partition_only)
+    part_graph = capture(partition_only, K)
     part_total, part_reps = timed(part_graph, args.window_seconds / 2)
+    del part_graph
     part_ms = part_total / (part_reps * K)
     peak, peak_src = measured_peak()
     achieved = local_bytes / (part_ms / 1e3) / 1e9
-    group = first.spec.num_heads // first.spec.num_kv_heads
+    group = gspec.num_heads // gspec.num_kv_heads
     kernel_name = "mma" if (args.kernel == "mma" or (args.kernel == "auto" and group >= 3)) \
         else "simt"
     traffic, traffic_src = committed_traffic(args.config, kernel_name)
+    if traffic is not None and strong:
+        global_bytes = job_bytes
+        traffic = int(traffic * local_bytes / max(global_bytes, 1))  # this rank's share
+        traffic_src += " (scaled to this rank's share of the batch)"
+
+    # Unroll convergence: per-step time of 32- and 128-step graphs.
+    conv = {}
+    for n in (32, 128):
+        g = capture(step, n)
+        tot, r = timed(g, 0.15, record=False)
+        conv[n] = tot * 1e3 / (r * n)
+        del g
+    convergence = abs(conv[32] - conv[128]) / conv[128]
 
     # e2e: public API with host buffers.  Each step's inputs (q, block table,
     # lengths) sit in one pinned staging buffer, copied to the device with one
@@ -574,8 +754,8 @@ def main():
             total += -(-n // 16) * 16
         dev = torch.empty(total, dtype=torch.uint8, device=device)
         views = [dev[o:o + n].view(t.dtype).view(t.shape) for o, n, t in zip(offs, sizes, parts)]
-        for v, t in zip(views, parts):
-            v.copy_(t)
+        for view, t in zip(views, parts):
+            view.copy_(t)
         w.q, w.table, w.lengths = views
         host = torch.empty(total, dtype=torch.uint8).pin_memory()
         host.copy_(dev)
@@ -583,10 +763,9 @@ def main():
 
     e2e_wls = list(wls)
     if len(e2e_wls) < 2:  # a second staging set for the same workload
-        import copy as _copy
-        twin = _copy.copy(first)
-        twin.q, twin.table, twin.lengths = (first.q.clone(), first.table.clone(),
-                                            first.lengths.clone())
+        twin = copy.copy(wls[0])
+        twin.q, twin.table, twin.lengths = (wls[0].q.clone(), wls[0].table.clone(),
+                                            wls[0].lengths.clone())
         e2e_wls.append(twin)
     stages = [staged(w) for w in e2e_wls]
     n_stage = len(stages)
@@ -637,7 +816,22 @@ def main():
     fault = ops.read_fault()
     clocks.stop()
 
+    if world > 1:  # shared if any rank's GPU is
+        flag = torch.tensor([1 if sharing["gpu_shared"] else 0], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        if sharing["gpu_shared"] is not None:
+            sharing["gpu_shared"] = bool(flag.item())
+
     if rank == 0:
+        parallelism = {
+            "single": "single GPU",
+            "head": f"KV-head-sharded x{world} (no collective on the data path)",
+            "batch": f"batch-sharded x{world}: token-balanced rows of one batch (no collective)",
+            "replica": f"independent batch per GPU x{world}",
+            "context": f"context-parallel x{world} (" + (
+                "one peer-memory exchange kernel over NVLink" if args.exchange == "p2p"
+                else "NCCL all-gather + LSE merge") + ")",
+        }[mode]
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -645,19 +839,12 @@ def main():
             "scaling": "strong" if strong else "weak", "vs_baseline": None,
             "dtype": "bf16 in, fp32 softmax/accumulate",
             "data": "synthetic (seeded N(0,1) BF16 q/K/V, shuffled page pool)",
-            "config": {"workload": args.config, "batch": first.spec.max_batch,
-                       "num_heads": first.spec.num_heads * (world if heads else 1),
-                       "num_kv_heads": first.spec.num_kv_heads * (world if heads else 1),
-                       "head_dim": first.spec.head_dim, "context": first.spec.max_context_len,
+            "config": {"workload": args.config, "batch": gspec.max_batch,
+                       "num_heads": gspec.num_heads, "num_kv_heads": gspec.num_kv_heads,
+                       "head_dim": gspec.head_dim, "context": gspec.max_context_len,
                        "splits": plan.splits, "tokens_per_split": plan.tokens_per_split,
-                       "kv_bytes_per_step": kv_bytes, "kernel": kernel_name,
-                       "parallelism": (f"context-parallel x{world} ("
-                                       + ("one peer-memory exchange kernel over NVLink"
-                                          if args.exchange == "p2p" else
-                                          "NCCL all-gather + LSE merge") + ")"
-                                       if context else f"KV-head-sharded x{world}" if heads
-                                       else f"batch-sharded x{world}" if world > 1
-                                       else "single GPU"),
+                       "kv_bytes_per_step": job_bytes, "kernel": kernel_name,
+                       "mode": mode, "parallelism": parallelism,
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",
                        "step": ("KV append (lengths += 1 on the device) + decode; KV bytes "
                                 "counted at the starting lengths" if args.append else "decode"),
@@ -668,22 +855,29 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "kernel_us": round(part_ms * 1e3, 3),
-                         "peak_source": peak_src, "traffic_source": traffic_src},
+                         "bytes_per_launch": local_bytes, "peak_source": peak_src,
+                         "traffic_source": traffic_src},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_call": round(e2e_ms / K * 1e3, 3),
-                    "api": ("paged_decode.parallel.ContextParallelDecode" if context
+                    "api": ("paged_decode.parallel.ContextParallelDecode" if mode == "context"
                             else "paged_decode.matched_splitkv.matched_decode")},
+            "convergence": {"us_per_step_unroll32": round(conv[32], 3),
+                            "us_per_step_unroll128": round(conv[128], 3),
+                            "delta": round(convergence, 4),
+                            "ok": convergence <= CONVERGENCE_LIMIT},
+            "parity": parity,
+            "gpu_shared": sharing["gpu_shared"],
+            "foreign_compute_apps": sharing["foreign_compute_apps"],
             # Own kernels per step: partition + merge; context mode adds the
             # local merge (nccl) or replaces both merges by the exchange (p2p).
-            "gpu_launches": (((3 if args.exchange == "nccl" else 2) if context else 2)
+            "gpu_launches": (((3 if args.exchange == "nccl" else 2) if mode == "context" else 2)
                              + (1 if args.append else 0)) * K * reps,
             "clocks": clocks.summary(windows),
             "fault_word": fault,
         }
         print(json.dumps(line), flush=True)
-    del step_graph, part_graph
-    if context:
+    if cp is not None:
         cp.close()
     if world > 1:
         dist.barrier()

@@ -12,7 +12,6 @@ that imports ``paged_decode.runtime`` / ``paged_decode.matched_splitkv`` /
   ops               tensor-level calls into the C ABI
   parallel          batch / KV-head / context sharding over NCCL
   kvcache           paged KV append (store_kvcache)
-  benchmark_protocol  graph-unrolled timing arithmetic
 
 GPU modules import torch lazily so the geometry contract works on CPU hosts.
 """

@@ -318,3 +318,25 @@ def shard_head_pool(k, v, q, rank, world, num_heads, num_kv_heads):
     kv_lo, kv_hi, q_lo, q_hi = head_shard(num_heads, num_kv_heads, world, rank)
     return (q[:, q_lo:q_hi].contiguous(), k[:, :, kv_lo:kv_hi].contiguous(),
             v[:, :, kv_lo:kv_hi].contiguous())
+
+
+def shard_batch_pool(k, v, table, lengths, rows):
+    """Rank-local pools and table for the batch rows `rows` (setup helper).
+
+    Only the live pages of those rows are copied, in row order, into a compact
+    local pool; the local table keeps the global width (padding -1) so the
+    geometry contract is unchanged.  Returns (k_local, v_local, table_local,
+    lengths_local).
+    """
+    idx = torch.as_tensor(rows, device=table.device, dtype=torch.long)
+    sub = table[idx]
+    lens = lengths[idx]
+    live = -(-lens.to(torch.int64) // PAGE_SIZE)
+    cols = torch.arange(table.shape[1], device=table.device)
+    mask = cols[None, :] < live[:, None]
+    pages = sub[mask].long()
+    local_table = torch.full_like(sub, -1)
+    local_table[mask] = torch.arange(pages.numel(), device=table.device, dtype=sub.dtype)
+    if pages.numel() == 0:
+        return k[:1].clone(), v[:1].clone(), local_table, lens.clone()
+    return k[pages].contiguous(), v[pages].contiguous(), local_table, lens.clone()

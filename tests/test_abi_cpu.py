@@ -16,7 +16,6 @@ import oracle
 from paged_decode import _lib
 from paged_decode.spec import DecodeSpec, validate_engine_options
 from paged_decode.splitkv_plan import make_splitkv_plan
-from paged_decode.benchmark_protocol import interval_per_operator, convergence_delta
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "pdl_b200.h"
@@ -141,19 +140,6 @@ def test_unsupported_explicit_counts(count):
 def test_unsupported_group():
     with pytest.raises(ValueError, match="16"):
         make_splitkv_plan(DecodeSpec(1, 32, 1, 256, 1024), 108)
-
-
-def test_graph_nodes_are_counted_as_logical_operators():
-    assert interval_per_operator(1.28, 10, 128) == 1.
-    assert interval_per_operator(1.28, 1280, 1) == 1.
-    assert convergence_delta(10.4, 10.) == pytest.approx(.04)
-
-
-@pytest.mark.parametrize('args', [(0., 10, 128), (float('nan'), 10, 128), (1., 0, 128),
-                                  (1., 10, 0), (1., 10, True)])
-def test_invalid_denominators_cannot_produce_latency(args):
-    with pytest.raises(ValueError):
-        interval_per_operator(*args)
 
 
 def test_b200_plan_invariants():

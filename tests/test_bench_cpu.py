@@ -32,9 +32,10 @@ def test_reference_arm_prints_one_contract_line():
                 "cpu_baseline", "e2e"):
         assert key in line, key
     assert line["impl"] == "reference" and line["higher_is_better"] is True
-    assert line["value"] > 0 and line["config"]["workload"] == "cfg2"
+    assert line["value"] > 0 and line["config"]["workload"] == "cfg4"
     cpu = line["cpu_baseline"]
     assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"]
+    assert cpu["blas"] and cpu["blas_threads_per_worker"] == 1 and cpu["workers"] == cpu["cores"]
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"],
                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
@@ -49,3 +50,17 @@ def test_exchange_micro_needs_several_ranks():
     rc, lines, _ = run_bench("--exchange-micro")
     assert rc == 0 and json.loads(lines[0]) == {
         "exchange_micro": "needs torchrun with 2 or more ranks"}
+
+
+def test_default_workload_and_modes():
+    """N=1 runs config 4 alone; N>1 splits one batch (strong scaling): by KV
+    head by default, by context for config 5."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    args = bench.parse_args([])
+    assert args.config == "cfg4" and args.mode == "auto"
+    assert bench.resolve_mode(args, 1) == "single"
+    assert bench.resolve_mode(args, 8) == "head"
+    assert bench.resolve_mode(bench.parse_args(["--config", "cfg5"]), 4) == "context"
+    assert bench.resolve_mode(bench.parse_args(["--mode", "batch"]), 2) == "batch"
+    assert bench.resolve_mode(bench.parse_args(["--mode", "replica"]), 2) == "replica"

@@ -209,3 +209,25 @@ def test_peer_exchange_handles_reach_every_rank():
     assert result[0] == expect and result[1] == expect
     with pytest.raises(ValueError):
         parallel.share_handles(b"short", 1)
+
+
+def test_shard_batch_pool_keeps_each_rows_pages():
+    """A rank's compact pool holds exactly its rows' live pages, in order, and
+    its table addresses them; padding stays -1."""
+    gen = torch.Generator().manual_seed(5)
+    lengths = torch.tensor([0, 700, 256, 1, 1024, 300], dtype=torch.int32)
+    width, pages = 4, 6 * 4
+    table = torch.randperm(pages, generator=gen).view(6, width).to(torch.int32)
+    k = torch.randn(pages, 256, 2, 8, generator=gen)
+    v = torch.randn(pages, 256, 2, 8, generator=gen)
+    for rows in ([1, 4], [0, 2, 5], [3]):
+        kl, vl, tl, ll = parallel.shard_batch_pool(k, v, table, lengths, rows)
+        assert torch.equal(ll, lengths[rows]) and tl.shape == (len(rows), width)
+        for i, row in enumerate(rows):
+            live = -(-int(lengths[row]) // 256)
+            for j in range(width):
+                if j < live:
+                    assert torch.equal(kl[tl[i, j]], k[table[row, j]])
+                    assert torch.equal(vl[tl[i, j]], v[table[row, j]])
+                else:
+                    assert int(tl[i, j]) == -1
