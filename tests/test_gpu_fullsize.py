@@ -3,9 +3,11 @@
 The NumPy oracle cannot gather a 524,288-token row in reasonable time, so
 at full size the checks are:
   * sampled rows of configs 2-5 (first/last rows, config 4's longest, median
-    and zero-length rows, both 524k-token rows of config 5) against an FP64
-    reference evaluated on the GPU in 64k-token chunks (oracle test
-    infrastructure), within the output tolerance of the parity tests;
+    and zero-length rows, both 524k-token rows of config 5; config 3 over its
+    batch and context grid) against an FP64 reference evaluated on the GPU in
+    64k-token chunks (oracle test infrastructure), within the output
+    tolerance of the parity tests, and every partition's LSE of those rows
+    against an FP64 logsumexp within the LSE tolerance;
   * size-independent properties, bit for bit: relocating every physical page
     (and rewriting the block table to match) leaves every output bit
     unchanged, and dynamic scheduling gives the bits of static scheduling.
@@ -15,8 +17,8 @@ this library's B200 plan otherwise.
 import pytest
 import torch
 
-from gpu_util import assert_out_close, requires_cuda
-from oracle.torch_reference import chunked_reference_rows
+from gpu_util import assert_lse_close, assert_out_close, requires_cuda
+from oracle.torch_reference import chunked_partition_lse, chunked_reference_rows
 from paged_decode import ops
 from paged_decode.matched_splitkv import allocate_matched_resources, matched_decode
 from paged_decode.splitkv_plan import make_b200_plan, make_splitkv_plan
@@ -50,16 +52,27 @@ def _free_memory():
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("name,batch", [("cfg2", None), ("cfg3", 32), ("cfg3", 128),
-                                        ("cfg4", None), ("cfg5", None)])
-def test_full_size_rows_match_fp64_reference(name, batch):
-    w = make_workload(name, device=DEV, batch=batch)
-    res = allocate_matched_resources(w.spec, DEV, plan=plan_for(name, w.spec))
+@pytest.mark.parametrize("name,batch,context", [
+    ("cfg2", None, None), ("cfg4", None, None), ("cfg5", None, None),
+    # Config 3's grid: B in {1, 8, 32, 128, 256}, contexts 528 and 2064.
+    ("cfg3", 1, 528), ("cfg3", 1, 2064), ("cfg3", 8, 528), ("cfg3", 8, 2064),
+    ("cfg3", 32, 528), ("cfg3", 32, 2064), ("cfg3", 128, 2064), ("cfg3", 256, 528),
+    ("cfg3", 256, 2064)])
+def test_full_size_rows_and_partition_lse_match_fp64_reference(name, batch, context):
+    """Sampled rows' outputs (max-abs 2^-7) and every partition's LSE of those
+    rows (1e-5 relative; see gpu_util) against FP64 references on the GPU."""
+    w = make_workload(name, device=DEV, batch=batch, context=context)
+    plan = plan_for(name, w.spec)
+    res = allocate_matched_resources(w.spec, DEV, plan=plan)
     out = matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res, scale=w.scale)
     rows = sample_rows(w)
     want = chunked_reference_rows(w.q, w.k, w.v, w.table, w.lengths, rows, scale=w.scale)
     assert_out_close(out[rows], want.float(), what=f"{name} rows {rows}")
     assert torch.isfinite(out.float()).all()
+    lse, mag = chunked_partition_lse(w.q, w.k, w.table, w.lengths, rows, plan.tokens_per_split,
+                                     plan.splits, scale=w.scale)
+    assert_lse_close(res.lse[rows], lse.cpu().numpy(), what=f"{name} lse rows {rows}",
+                     score_mag=mag.cpu().numpy())
 
 
 @pytest.mark.parametrize("name", ["cfg4", "cfg5"])

@@ -107,3 +107,66 @@ def test_graph_captured_decode_loop_with_device_lengths():
         expected = oracle.dense_reference(new_q[s].float().cpu().numpy(), kh, vh, th, n)
         assert_out_close(outs[s], expected, f"step {s}")
     del graph
+
+
+def test_config3_decode_loop_of_256_steps_in_one_graph():
+    """BASELINE config 3's protocol at its full shape: B=32, Hq=16, Hkv=4,
+    D=256 (2% of K channels x8), context 528 -> 784.  Every step appends each
+    row's new K/V token at its length (lengths += 1 on the device) and
+    decodes; the 256 steps are captured once in a CUDA graph and replayed.
+    Steps 0, 128 and 255 of sampled rows match the FP64 reference (outputs
+    max-abs 2^-7), and the graph's outputs equal an eager run's bit for bit."""
+    from oracle.torch_reference import chunked_reference_rows
+    from paged_decode import ops
+    from paged_decode.splitkv_plan import make_b200_plan
+    from paged_decode.workloads import make_workload
+    w = make_workload("cfg3", device="cuda", batch=32, context=528)
+    steps, rows = 256, [0, 13, 31]
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    new_k = torch.randn(steps, 32, 4, 256, generator=gen, device="cuda").to(torch.bfloat16)
+    new_v = torch.randn_like(new_k)
+    res = allocate_matched_resources(w.spec, "cuda",
+                                     plan=make_b200_plan(w.spec, ops.sm_count("cuda")))
+    k0, v0, len0 = w.k.clone(), w.v.clone(), w.lengths.clone()
+
+    def restore():
+        w.k.copy_(k0)
+        w.v.copy_(v0)
+        w.lengths.copy_(len0)
+
+    def loop(hist, n):
+        for i in range(n):
+            append_decode_kv(new_k[i], new_v[i], w.k, w.v, w.table, w.lengths)
+            hist[i].copy_(matched_decode(w.q, w.k, w.v, w.table, w.lengths, resources=res,
+                                         scale=w.scale))
+
+    eager = torch.empty(steps, 32, 16, 256, dtype=torch.bfloat16, device="cuda")
+    loop(eager, steps)
+    restore()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        warm = torch.empty(3, 32, 16, 256, dtype=torch.bfloat16, device="cuda")
+        loop(warm, 3)
+    torch.cuda.current_stream().wait_stream(side)
+    restore()
+    replayed = torch.empty_like(eager)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loop(replayed, steps)
+    restore()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(w.lengths, len0 + steps)
+    assert torch.equal(replayed, eager)
+    for i in (0, 128, 255):
+        # The cache as step i sees it: the original pages plus tokens 0..i.
+        k, v = k0.clone(), v0.clone()
+        for j in range(i + 1):
+            pos = len0 + j
+            pages = w.table[torch.arange(32, device="cuda"), (pos // 256).long()].long()
+            k[pages, (pos % 256).long()] = new_k[j]
+            v[pages, (pos % 256).long()] = new_v[j]
+        want = chunked_reference_rows(w.q, k, v, w.table, len0 + i + 1, rows, scale=w.scale)
+        assert_out_close(replayed[i][rows], want.float(), what=f"step {i} rows {rows}")
+    del graph
