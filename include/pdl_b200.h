@@ -140,8 +140,9 @@ typedef struct PdlDecodeArgs {
 /* Partition kernel: per (row, KV head, partition) online softmax over the
  * partition's tokens for every query head of the group; writes the split
  * workspace in args->protocol.  Only partitions holding live tokens are
- * computed; empty ones are stored as such (unless PDL_FLAG_SKIP_EMPTY).  With tokens_per_split == 0 and splits == 1 it
- * writes the normalised output to args->out directly and needs no workspace.
+ * computed; empty ones are stored as such (unless PDL_FLAG_SKIP_EMPTY).
+ * With tokens_per_split == 0 and splits == 1 it writes the normalised output
+ * to args->out directly and needs no workspace.
  * Replaces _normalized_partition (reference src/paged_decode/matched_splitkv.py:52-98),
  * _split (src/paged_decode/kernels.py:44-80), _tc_partition
  * (src/paged_decode/tc_splitk.py:13-60), _base (src/paged_decode/kernels.py:10-41)
@@ -350,8 +351,13 @@ const char *pdl_last_error(void);
 int pdl_abi_version(void);
 
 /* Sticky device-side fault word of the current device (0 = none); a
- * non-zero value records which bounded wait gave up.  Synchronises the
- * device; for diagnostics only, never on a hot path. */
+ * non-zero value records which bounded wait gave up (bits: 1 producer
+ * waiting for a free stage, 2 consumer waiting for a tile, 4 draining copies
+ * at exit, 8 misaligned shared memory, 16 exchange peer).  The outputs and
+ * workspaces of every launch since the word was last cleared are then
+ * undefined: a CTA that gives up stops processing, and an item it had
+ * already claimed is processed by nobody.  Synchronises the device; for
+ * diagnostics only, never on a hot path. */
 int pdl_read_fault(uint32_t *fault, int clear);
 
 #ifdef __cplusplus

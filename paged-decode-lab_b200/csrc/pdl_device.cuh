@@ -69,6 +69,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking check whether the phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bring the 128-byte line holding `addr` into L1 ahead of its load.
+__device__ __forceinline__ void prefetch_l1(const void *addr) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(addr));
+}
+
 // Wait for the phase with the given parity.  Gives up after WAIT_LIMIT_NS,
 // records `code` in the fault word and returns false; the caller then stops
 // issuing work and exits.  A healthy pipeline never reaches the slow path.

@@ -15,11 +15,12 @@
 //       BF16 hi + lo parts (two MMAs) so P.V keeps FP32-level accuracy.
 //
 // Consumer warps come in NG token groups of DS warps.  Each group owns 16*MT
-// rows of every T-token tile and its own running (m, l, O); at D = 256 the
-// two warps of a group (DS = 2) both compute the group's scores (identical
-// instructions on identical data, so identical m, l and P) and each keeps
-// the O columns of its half of D, halving the P.V work per warp without any
-// exchange between them.  The groups are merged at the end of an item
+// rows of every T-token tile and its own running (m, l, O).  At D = 256 the
+// two warps of a group (DS = 2) split D: each multiplies its half of D for
+// the scores, the two halves are exchanged through shared memory and added
+// (s_a + s_b in one warp, s_b + s_a in the other: the same bits), so both
+// warps hold identical scores, m, l and P; each then keeps the O columns of
+// its half of D.  The q.k and P.V work per warp are both halved.  The groups are merged at the end of an item
 // through shared memory (combine_and_store).  Rows outside the partition or beyond
 // the live length are masked: scores to -inf, V fragment halves to zero
 // (dead page slots may hold NaN).
@@ -43,6 +44,7 @@ struct MmaShape {
   static constexpr int MT = TW / 16;                               // 16-row MMA tiles per warp
   static constexpr int KS = D / 16;                                // 16-column slices of D
   static constexpr int KSW = KS / DS;                              // slices of O per warp
+  static constexpr int KQ = KS / DS;                               // slices of q.k per warp
   static constexpr int SUB_BYTES = T * 128;
   static constexpr int TILE_BYTES = T * D * 2;
   static constexpr int NTHREADS = 32 * (NC + 1);
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
   constexpr int NS = MmaStages<D, GC>::NS;
   using L = PartitionSmem<D, S::T, NS, S::NG, GC>;
   constexpr int NC = S::NC, NG = S::NG, DS = S::DS, T = S::T, TW = S::TW, MT = S::MT;
-  constexpr int KS = S::KS, KSW = S::KSW;
+  constexpr int KSW = S::KSW, KQ = S::KQ;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *kbuf = smem;
@@ -170,8 +172,9 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       store_fill<D>(p, w, h0, rows, tid, NC * 32);
       continue;
     }
-    // q of head (nt*8 + grp) as B fragments: dims kk*16 + quad*2 + {0,1} and +8.
-    uint32_t qf[NT][KS][2];
+    // q of head (nt*8 + grp) as B fragments for this warp's slices of D
+    // (kk = dh * KQ + kq): dims kk*16 + quad*2 + {0,1} and +8.
+    uint32_t qf[NT][KQ][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int hl = nt * 8 + grp;
@@ -179,9 +182,10 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       const __nv_bfloat16 *qrow =
           p.q + (int64_t)w.b * p.q_stride_batch + (int64_t)(h0 + (valid ? hl : 0)) * p.q_stride_head;
 #pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        qf[nt][kk][0] = valid ? load_q_pair(qrow + kk * 16 + quad * 2, q_vec) : 0u;
-        qf[nt][kk][1] = valid ? load_q_pair(qrow + kk * 16 + quad * 2 + 8, q_vec) : 0u;
+      for (int kq = 0; kq < KQ; ++kq) {
+        const int kk = dh * KQ + kq;
+        qf[nt][kq][0] = valid ? load_q_pair(qrow + kk * 16 + quad * 2, q_vec) : 0u;
+        qf[nt][kq][1] = valid ? load_q_pair(qrow + kk * 16 + quad * 2 + 8, q_vec) : 0u;
       }
     }
 
@@ -208,9 +212,10 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       if (r0 < hi && r0 + TW > lo) {
         const uint32_t ks = kbase + s * S::TILE_BYTES;
         const uint32_t vs = vbase + s * S::TILE_BYTES;
-        // ---- S^T = K . Q^T, accumulated in CH independent chains (slices of D
-        // interleaved) so consecutive MMAs do not wait on each other.
-        constexpr int CH = KS >= 16 ? 4 : 2;
+        // ---- S^T = K . Q^T over this warp's slices of D, accumulated in CH
+        // independent chains (slices interleaved) so consecutive MMAs do not
+        // wait on each other.
+        constexpr int CH = KQ >= 16 ? 4 : 2;
         float part[CH][MT][NT][4];
 #pragma unroll
         for (int c = 0; c < CH; ++c)
@@ -220,15 +225,15 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
             for (int nt = 0; nt < NT; ++nt)
               part[c][mt][nt][0] = part[c][mt][nt][1] = part[c][mt][nt][2] = part[c][mt][nt][3] = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          const int chunk = kk * 2 + k_chunk;
+        for (int kq = 0; kq < KQ; ++kq) {
+          const int chunk = (dh * KQ + kq) * 2 + k_chunk;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             uint32_t a[4];
             ldsm_x4(ks + (chunk >> 3) * S::SUB_BYTES + swizzle128(r0 + mt * 16 + k_row, chunk & 7), a);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-              mma_bf16(part[kk % CH][mt][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+              mma_bf16(part[kq % CH][mt][nt], a, qf[nt][kq][0], qf[nt][kq][1]);
           }
         }
         float sc[MT][NT][4];
@@ -243,6 +248,39 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
               for (int c = 1; c < CH; ++c) v += part[c][mt][nt][e];
               sc[mt][nt][e] = v;
             }
+        if constexpr (DS == 2) {
+          // Exchange the halves with the other warp of the pair through a
+          // slot of the combine area (unused during the tiles), double
+          // buffered by tile parity so a warp one tile ahead never overwrites
+          // what its partner still reads.
+          constexpr int E = MT * NT * 4;
+          static_assert(NG * 2 * 2 * 32 * E <= NG * GC * D, "exchange slots fit the combine area");
+          float *xmine = comb_acc + ((((tg * 2 + dh) * 2 + (i & 1)) * 32) + lane) * E;
+          const float *xpeer = comb_acc + ((((tg * 2 + (dh ^ 1)) * 2 + (i & 1)) * 32) + lane) * E;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              *reinterpret_cast<float4 *>(xmine + (mt * NT + nt) * 4) =
+                  make_float4(sc[mt][nt][0], sc[mt][nt][1], sc[mt][nt][2], sc[mt][nt][3]);
+          // One named barrier per pair (ids 2, 3: compile-time constants, so
+          // the kernel reserves 4 barriers, not all 16).
+          static_assert(NG == 2, "pair barriers 2 and 3");
+          if (tg == 0)
+            named_barrier(2, 64);
+          else
+            named_barrier(3, 64);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const float4 o = *reinterpret_cast<const float4 *>(xpeer + (mt * NT + nt) * 4);
+              sc[mt][nt][0] += o.x;
+              sc[mt][nt][1] += o.y;
+              sc[mt][nt][2] += o.z;
+              sc[mt][nt][3] += o.w;
+            }
+        }
         // ---- mask rows outside [lo, hi) and fold in the scale (base 2)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
@@ -333,6 +371,9 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     }
 
     // ---- per-warp state -> shared memory, then merge the warps
+    // (at D = 256 the combine area held the score exchange: every pair is
+    // done with it first)
+    if constexpr (DS == 2) named_barrier(1, NC * 32);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -360,7 +401,22 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
         }
       }
     }
+    ring_peek(ring, ik, cw == 0 && lane == 0);
     named_barrier(1, NC * 32);
+    {
+      // The next item's q rows into L1 while this one is combined (each of a
+      // row's D/64 lines by one of the four lanes that load it).
+      const WorkItem nx = peeked_item(ring, ik);
+      if (nx.kind == ITEM_COMPUTE) {
+        int nh0, nrows;
+        item_heads<GC>(p, nx.hs, nh0, nrows);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          if (nt * 8 + grp < nrows)
+            prefetch_l1(p.q + (int64_t)nx.b * p.q_stride_batch +
+                        (int64_t)(nh0 + nt * 8 + grp) * p.q_stride_head + (quad % (D / 64)) * 64);
+      }
+    }
     combine_and_store<D, GC, NG, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
   }

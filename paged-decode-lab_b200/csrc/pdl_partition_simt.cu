@@ -247,7 +247,21 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         comb_ml[cw * 2 * GC + GC + g] = l[g];
       }
     }
+    ring_peek(ring, ik, cw == 0 && lane == 0);
     named_barrier(1, NC * 32);
+    {
+      // The next item's q chunks into L1 while this one is combined.
+      const WorkItem nx = peeked_item(ring, ik);
+      if (nx.kind == ITEM_COMPUTE) {
+        int nh0, nrows;
+        item_heads<GC>(p, nx.hs, nh0, nrows);
+#pragma unroll
+        for (int g = 0; g < GC; ++g)
+          if (g < nrows)
+            prefetch_l1(p.q + (int64_t)nx.b * p.q_stride_batch +
+                        (int64_t)(nh0 + g) * p.q_stride_head + j * 8);
+      }
+    }
     combine_and_store<D, GC, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
   }

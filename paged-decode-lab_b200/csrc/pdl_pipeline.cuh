@@ -66,8 +66,7 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
 // same schedule from the row lengths, so partitions past a row's length cost
 // no claim and no consumer round trip.  The order balances like
 // longest-first under dynamic scheduling:
-//   1. every FULL partition (tokens_per_split tokens), partition-major: every
-//      row's partition 0, then every row's partition 1, ...;
+//   1. every FULL partition (tokens_per_split tokens), row-major;
 //   2. every row's last, PARTIAL partition, in four size classes, largest
 //      first (in direct mode each row is one partial partition);
 //   3. FILL items storing the empty partitions, in chunks of fill_splits
@@ -75,25 +74,28 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
 //      zero-length row), last, so idle CTAs take them.
 // Items of 1 and 2 are expanded over the (KV head, sub-group) pairs, which
 // vary fastest, so concurrent CTAs read neighbouring bytes of the same
-// pages.  Decoding an item of partition s costs a few warp ballots per
-// partition index up to s (partitions that every row has are decoded
-// directly), and no prefix sums, so a CTA's first item -- nearly always in
-// partition 0 -- is known right after the lengths arrive.  For a batch of
-// equal lengths the order is the dense partition-major one, which lets the
+// pages.  One prefix sum over the rows' full-partition counts, at set-up,
+// makes decoding any item a few warp ballots.  For rows that all hold
+// full partitions only, the order is the dense row-major one, which lets the
 // producer request the first item's block-table entries with the lengths.
 //
 // The code is kept small on purpose: the producer runs it once per item, so
 // it is rarely in the instruction cache, and rolled loops over the batch's
 // row chunks (the per-row arrays then live in L1-cached local memory) cost
 // far less than fully unrolled ones -- measured on B200, unrolling all 16
-// chunks added 4 to 40 us to short launches.
+// chunks added 4 to 40 us to short launches.  A partition-major order was
+// tried as well: decoding its items needs one ballot pass per partition
+// index, which made launches of many partitions the producer's bottleneck
+// (config 4 in 1024-token partitions: 642 vs 505 us).
 constexpr int RMAX = 16;  // rows per lane: batches up to 512 rows use this schedule
 
 struct LiveSchedule {
   int len[RMAX];   // clamped length of row r * 32 + lane (0 past the batch)
   int full[RMAX];  // its full partitions
+  int fpre[RMAX];  // exclusive row-major prefix of full partitions
   int cls[RMAX];   // size class of its partial partition, -1 if none
   int R;           // row chunks of the batch
+  int nfull;       // full partitions of the batch
 };
 
 // The launch parameters the schedule depends on (passed by value, so the
@@ -131,6 +133,16 @@ __device__ __forceinline__ int warp_sum(int v) {
   return v;
 }
 
+// Inclusive prefix over the warp's lanes.
+__device__ __forceinline__ int warp_scan(int x, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(FULL_MASK, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
 static __device__ __noinline__ void build_schedule(const SchedParams p, int lane, LiveSchedule &s) {
   const int tps = p.tps;
   s.R = (p.batch + 31) >> 5;
@@ -150,25 +162,31 @@ static __device__ __noinline__ void build_schedule(const SchedParams p, int lane
     span = max(1, maxlen);
   }
   const float inv_span = 4.f / (float)span;
+  int carry = 0;
 #pragma unroll 1
   for (int r = 0; r < s.R; ++r) {
-    s.full[r] = s.len[r] / tps;
-    const int rem = s.len[r] - s.full[r] * tps;
+    const int f = s.len[r] / tps;
+    const int rem = s.len[r] - f * tps;
+    s.full[r] = f;
+    const int x = warp_scan(f, lane);
+    s.fpre[r] = carry + x - f;
+    carry += __shfl_sync(FULL_MASK, x, 31);
     s.cls[r] = rem > 0 ? min(3, (int)((float)(span - rem) * inv_span)) : -1;
   }
+  s.nfull = carry;
 }
 
 // Items of the schedule: (full + partial partitions) * heads + fill chunks.
 static __device__ __noinline__ int schedule_total(const SchedParams p, const LiveSchedule &s,
                                                   int lane) {
-  int parts = 0, fills = 0;
+  int partial = 0, fills = 0;
 #pragma unroll 1
   for (int r = 0; r < s.R; ++r) {
     const int live = s.full[r] + (s.cls[r] >= 0 ? 1 : 0);
-    parts += live;
+    partial += s.cls[r] >= 0 ? 1 : 0;
     fills += fill_chunks(p, r * 32 + lane, s.len[r], live);
   }
-  return warp_sum(parts) * p.heads + warp_sum(fills);
+  return (s.nfull + warp_sum(partial)) * p.heads + warp_sum(fills);
 }
 
 // Item `item` of the schedule (every lane returns the same item); STOP past
@@ -180,65 +198,48 @@ static __device__ __noinline__ WorkItem decode_live(const SchedParams p, const L
   const int heads = p.heads;
   const int u = item / heads;
   const int hs = item - u * heads;
-  int before = 0;  // row partitions of earlier groups
-  // 1. Full partitions, partition-major.  Partitions that every row has
-  // (below the smallest full count) are decoded directly.
-  int split = 0;
-  if (u >= p.batch) {
-    int fmin = INT_MAX;
+  // 1. Full partitions, row-major: the row whose range [fpre, fpre + full) holds u.
+  if (u < s.nfull) {
 #pragma unroll 1
-    for (int r = 0; r < s.R; ++r)
-      if (r * 32 + lane < p.batch) fmin = min(fmin, s.full[r]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) fmin = min(fmin, __shfl_xor_sync(FULL_MASK, fmin, o));
-    if ((int64_t)u < (int64_t)p.batch * fmin) {
-      w.kind = ITEM_COMPUTE;
-      w.hs = hs;
-      w.b = u % p.batch;
-      w.split = u / p.batch;
-      w.start = w.split * tps;
-      w.stop = w.start + tps;
-      return w;
-    }
-    split = fmin;
-    before = p.batch * fmin;
-  }
-  // Group g < 0: full partitions of partition index `split`, one index after
-  // the other while any row has them; g = 0..3: partial partitions of size
-  // class g.  Rows of a group are taken in row order.
-  for (int g = -1; g < 4; ++g) {
-    int n_all;
-    do {
-      int k = u - before;
-      n_all = 0;
-#pragma unroll 1
-      for (int r = 0; r < s.R; ++r) {
-        const bool in = g < 0 ? s.full[r] > split : s.cls[r] == g;
-        const uint32_t m = __ballot_sync(FULL_MASK, in);
-        const int n = __popc(m);
-        if (k < n) {
-          const int src = nth_set_bit(m, k);
-          w.kind = ITEM_COMPUTE;
-          w.hs = hs;
-          w.b = r * 32 + src;
-          if (g < 0) {
-            w.split = split;
-            w.start = split * tps;
-            w.stop = w.start + tps;
-          } else {
-            const int len = __shfl_sync(FULL_MASK, s.len[r], src);
-            w.split = len / tps;
-            w.start = w.split * tps;
-            w.stop = len;
-          }
-          return w;
-        }
-        k -= n;
-        n_all += n;
+    for (int r = 0; r < s.R; ++r) {
+      const uint32_t m =
+          __ballot_sync(FULL_MASK, s.full[r] > 0 && s.fpre[r] <= u && u < s.fpre[r] + s.full[r]);
+      if (m) {
+        const int src = __ffs(m) - 1;
+        w.kind = ITEM_COMPUTE;
+        w.hs = hs;
+        w.b = r * 32 + src;
+        w.split = u - __shfl_sync(FULL_MASK, s.fpre[r], src);
+        w.start = w.split * tps;
+        w.stop = w.start + tps;
+        return w;
       }
-      before += n_all;
-      ++split;
-    } while (g < 0 && n_all > 0);
+    }
+    return w;  // not reached: u lies in some row's range
+  }
+  // 2. Partial partitions, largest class first.
+  int before = s.nfull;
+  for (int g = 0; g < 4; ++g) {
+    int k = u - before, n_all = 0;
+#pragma unroll 1
+    for (int r = 0; r < s.R; ++r) {
+      const uint32_t m = __ballot_sync(FULL_MASK, s.cls[r] == g);
+      const int n = __popc(m);
+      if (k < n) {
+        const int src = nth_set_bit(m, k);
+        const int len = __shfl_sync(FULL_MASK, s.len[r], src);
+        w.kind = ITEM_COMPUTE;
+        w.hs = hs;
+        w.b = r * 32 + src;
+        w.split = len / tps;
+        w.start = w.split * tps;
+        w.stop = len;
+        return w;
+      }
+      k -= n;
+      n_all += n;
+    }
+    before += n_all;
   }
   // 3. Fill chunks, row-major (a prefix sum over the rows' chunk counts).
   const int j = item - before * heads;
@@ -247,12 +248,7 @@ static __device__ __noinline__ WorkItem decode_live(const SchedParams p, const L
   for (int r = 0; r < s.R; ++r) {
     const int live = s.full[r] + (s.cls[r] >= 0 ? 1 : 0);
     const int c = fill_chunks(p, r * 32 + lane, s.len[r], live);
-    int x = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(FULL_MASK, x, o);
-      if (lane >= o) x += y;
-    }
+    const int x = warp_scan(c, lane);
     const int pre = carry + x - c;
     const uint32_t m = __ballot_sync(FULL_MASK, c > 0 && pre <= j && j < pre + c);
     if (m) {
@@ -327,6 +323,7 @@ struct ItemRing {
   uint64_t *empty;       // [IR] consumers -> producer, count 1 (the leader)
   volatile int *slot;    // [IR][8] published items (WorkItem fields)
   volatile int *stop;    // the leader's "stop" decision for the current item
+  volatile int *peek;    // the leader's look at the next slot: published already?
 };
 
 __device__ __forceinline__ void ring_init(const ItemRing &r) {
@@ -389,6 +386,26 @@ __device__ __forceinline__ WorkItem consumer_next(const ItemRing &r, uint32_t &k
   return w;
 }
 
+// While the consumers finish item k, the leader checks -- without waiting --
+// whether item k + 1 is already published (it usually is: the producer runs
+// ahead); after the next named barrier every consumer thread may read it and
+// prefetch that item's q rows into L1, so the q loads at its start do not
+// wait for L2.  `k` is the ring index consumer_next will use next.
+__device__ __forceinline__ void ring_peek(const ItemRing &r, uint32_t k, bool leader) {
+  if (leader) *r.peek = mbar_test_wait(&r.full[k % IR], (k / IR) & 1) ? 1 : 0;
+}
+
+__device__ __forceinline__ WorkItem peeked_item(const ItemRing &r, uint32_t k) {
+  WorkItem w = stop_item();
+  if (*r.peek) {
+    const volatile int *src = r.slot + 8 * (k % IR);
+    w.kind = src[0];
+    w.b = src[1];
+    w.hs = src[4];
+  }
+  return w;
+}
+
 // ------------------------------------------------------------- producer
 // Producer warp: walks this CTA's items -- blockIdx.x first, then (dynamic
 // scheduling) gridDim.x + the next value of a global atomic counter, or
@@ -419,14 +436,14 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
   const SchedParams sp = sched_params(p);
   LiveSchedule sched;
   // Live schedule: the first item's block-table entries are requested before
-  // the lengths arrive, for the dense partition-major guess (row u % batch,
-  // partition u / batch with u = item / heads), which the live order equals
-  // when every row has the same length.
+  // the lengths arrive, for the dense row-major guess (row u / splits,
+  // partition u % splits with u = item / heads), which the live order equals
+  // when every row fills the table's capacity with full partitions.
   int guess_row = -1, guess_base = -1, guess_page = 0;
   if (live) {
     const int u0 = item / heads;
-    guess_row = u0 % p.batch;
-    const int64_t first_tok = (int64_t)(u0 / p.batch) * p.tokens_per_split;
+    guess_row = min(u0 / p.splits, p.batch - 1);
+    const int64_t first_tok = (int64_t)(u0 % p.splits) * p.tokens_per_split;
     guess_base = first_tok < (int64_t)row_capacity(p) ? (int)(first_tok >> 8) : -1;
     if (guess_base >= 0 && guess_base + lane < p.table_width)
       guess_page = __ldg(p.table + (int64_t)guess_row * p.table_stride + guess_base + lane);
@@ -681,6 +698,7 @@ __device__ __forceinline__ ItemRing item_ring(uint8_t *smem) {
   r.empty = r.full + IR;
   r.slot = reinterpret_cast<volatile int *>(smem + L::SLOT_OFFSET);
   r.stop = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET) + 1;
+  r.peek = reinterpret_cast<volatile int *>(smem + L::FLAG_OFFSET) + 2;
   return r;
 }
 

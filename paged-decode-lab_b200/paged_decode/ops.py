@@ -155,6 +155,23 @@ def lse_merge(margs, device):
         raise RuntimeError(f"pdl_lse_merge failed: {_lib.status_text(status)}")
 
 
+FAULT_BITS = {1: "producer waited too long for a free stage",
+              2: "consumer waited too long for a tile",
+              4: "copies in flight did not land at exit",
+              8: "dynamic shared memory misaligned",
+              16: "exchange peer did not arrive in time"}
+
+
+def check_fault(clear=True):
+    """Raise if a bounded device-side wait gave up since the last clear: the
+    outputs of those launches are undefined.  Synchronises; not for hot paths."""
+    word = _lib.read_fault(clear)
+    if word:
+        names = [name for bit, name in FAULT_BITS.items() if word & bit]
+        raise RuntimeError(f"device fault word {word:#x}: {'; '.join(names)} -- outputs of the "
+                           "launches since the last clear are undefined")
+
+
 def read_fault(clear=False):
     """Device-side fault word (bounded waits that gave up); synchronises."""
     return _lib.read_fault(clear)
