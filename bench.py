@@ -28,10 +28,9 @@ plan (8 partitions of 4096 tokens, dynamic scheduling).
 * ``--impl reference``: that CPU implementation alone, on all host cores.
 
 Multi-GPU (torchrun), ``--mode``:
-  head     (default) one global batch, KV heads split over the ranks, no
-           collective on the data path ("scaling": "strong");
-  batch    one global batch, rows split token-balanced over the ranks
-           ("strong");
+  batch    (default) one global batch, rows split token-balanced over the
+           ranks, no collective on the data path ("scaling": "strong");
+  head     one global batch, KV heads split over the ranks ("strong");
   context  one global batch, each row's pages split over the ranks, one
            exchange of (partial, LSE) per step (default for cfg5; "strong");
   replica  every rank decodes its own batch ("weak").
@@ -76,9 +75,9 @@ def parse_args(argv=None):
     ap.add_argument("--splits", type=int, default=None, help="matched plan split count")
     ap.add_argument("--kernel", default="auto", choices=("auto", "simt", "mma"))
     ap.add_argument("--mode", default="auto", choices=("auto", "head", "batch", "context", "replica"),
-                    help="N>1: split one batch by KV head, by rows or by context (strong "
+                    help="N>1: split one batch by rows, by KV head or by context (strong "
                          "scaling), or run an independent batch per rank (weak); auto = context "
-                         "for cfg5, else head")
+                         "for cfg5, else batch")
     ap.add_argument("--exchange", default="p2p", choices=("nccl", "p2p"),
                     help="context mode: NCCL all-gather between two merge kernels, or one "
                          "kernel storing into peers' buffers over NVLink (pdl_exchange_merge)")
@@ -109,7 +108,7 @@ def resolve_mode(args, world):
         return "single"
     if args.mode != "auto":
         return args.mode
-    return "context" if args.config == "cfg5" else "head"
+    return "context" if args.config == "cfg5" else "batch"
 
 
 def sweep(reps=20):

@@ -53,14 +53,14 @@ def test_exchange_micro_needs_several_ranks():
 
 
 def test_default_workload_and_modes():
-    """N=1 runs config 4 alone; N>1 splits one batch (strong scaling): by KV
-    head by default, by context for config 5."""
+    """N=1 runs config 4 alone; N>1 splits one batch (strong scaling): by rows
+    by default, by context for config 5."""
     sys.path.insert(0, str(ROOT))
     import bench
     args = bench.parse_args([])
     assert args.config == "cfg4" and args.mode == "auto"
     assert bench.resolve_mode(args, 1) == "single"
-    assert bench.resolve_mode(args, 8) == "head"
+    assert bench.resolve_mode(args, 8) == "batch"
     assert bench.resolve_mode(bench.parse_args(["--config", "cfg5"]), 4) == "context"
-    assert bench.resolve_mode(bench.parse_args(["--mode", "batch"]), 2) == "batch"
+    assert bench.resolve_mode(bench.parse_args(["--mode", "head"]), 2) == "head"
     assert bench.resolve_mode(bench.parse_args(["--mode", "replica"]), 2) == "replica"
