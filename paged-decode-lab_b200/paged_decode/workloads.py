@@ -10,7 +10,8 @@ scatter each row over a shuffled pool.  Tensors are generated on the device
   cfg3  Hq=16, Hkv=4,         D=256, ctx 528 | 2064, B in {1,8,32,128,256},
         capacity 2320 (room for 256 decode steps), 2% of K channels x8
   cfg4  B=128, Hq=32, Hkv=8,  D=128, len ~ lognormal(median 4096, sigma 1)
-        clipped to [1, 32768], every 32nd row 0 (seed 20261201: sum 750,637)
+        clipped to [1, 32768], every 32nd row 0 (seed 20261201: sum 750,637);
+        a smaller batch takes the first rows of the same draw
   cfg5  B=2,   Hq=64, Hkv=8,  D=128, ctx 524288 (2048 pages per row)
 """
 from dataclasses import dataclass, field
@@ -97,8 +98,10 @@ def make_workload(name, device="cuda", seed=0, batch=None, context=None, rank=0)
         lengths = torch.full((b,), ctx, dtype=torch.int32, device=device)
         meta = dict(outlier_channels=int(channels.numel()))
     elif name == "cfg4":
-        b, hq, hkv, d, cap = 128, 32, 8, 128, 32768
-        lens_np = cfg4_lengths()
+        # `batch` (default 128) takes the first rows of the same draw, e.g. a
+        # smaller case of the same lengths for profiling.
+        b, hq, hkv, d, cap = batch or 128, 32, 8, 128, 32768
+        lens_np = cfg4_lengths(batch=b)
         lengths = torch.from_numpy(lens_np).to(device)
         need = [-(-int(n) // PAGE) for n in lens_np]
         pool = max(1, sum(need))
