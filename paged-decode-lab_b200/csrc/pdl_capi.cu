@@ -270,9 +270,12 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   p.mode = mode;
   p.q_vec16 = aligned(a->q, 16) && (a->q_stride_batch % 8 == 0) && (a->q_stride_head % 8 == 0);
   p.write_empty = (a->flags & PDL_FLAG_SKIP_EMPTY) ? 0 : 1;
-  // A fill item stores about 16 KB: whole empty partitions of all heads of a row.
+  // A fill item stores whole empty partitions of all heads of a row, about
+  // 128 KB: a launch's fills then take a few items per row, not one per
+  // partition (each item costs the producer a schedule decode, microseconds
+  // that fills of a few KB cannot hide).
   p.fill_splits =
-      (int)std::max<int64_t>(1, 16384 / ((int64_t)a->num_heads * (a->head_dim + 1) * 4));
+      (int)std::max<int64_t>(1, 131072 / ((int64_t)a->num_heads * (a->head_dim + 1) * 4));
   p.out = static_cast<__nv_bfloat16 *>(a->out);
   p.partial = a->partial;
   p.lse = a->lse;

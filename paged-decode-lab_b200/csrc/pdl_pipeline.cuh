@@ -474,7 +474,8 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
         w = decode_dense(p, item, p.sched != nullptr, lane, skip, base, my_page);
       }
     }
-    if (w.kind == ITEM_STOP) {
+    // A skipped item (empty, its partition not stored) moves on to the next.
+    if (w.kind == ITEM_STOP && !skip) {
       publish(ring, k, w, p.fault, abort_flag, lane);
       break;
     }

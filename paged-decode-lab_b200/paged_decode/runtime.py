@@ -171,12 +171,19 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
     # checks, not the instructions that compute the result.
     kernel = "mma" if tensor_cores else "auto"
     if split:
+        # The (m, l, acc) workspace is this call's scratch: the merge reads the
+        # ceil(length / 1024) live partitions of each row only, so partitions
+        # past a row's length are not written (the reference stores -inf, 0, 0
+        # there for its merge, which reads all of them).  Writing them costs
+        # about 9% at config 4's 32 partitions: 55 MB of stores per call,
+        # 486 vs 447 us measured on B200.
+        flags = ops.FLAG_SKIP_EMPTY | (0 if resources.counters is None else ops.FLAG_DYNAMIC)
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale,
                                tokens_per_split=PARTITION_SIZE, splits=spec.partitions,
                                protocol=ops.PROTOCOL_MLA, kernel=kernel, out=resources.out,
                                maxima=resources.maxima, denoms=resources.denoms,
                                accums=resources.accums, counters=resources.counters,
-                               flags=0 if resources.counters is None else ops.FLAG_DYNAMIC)
+                               flags=flags)
     else:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)

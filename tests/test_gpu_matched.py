@@ -234,7 +234,9 @@ def test_every_partition_slot_follows_the_workspace_contract(kernel, protocol, f
 def test_batches_past_the_register_schedule(kernel, rows):
     """Up to 512 rows the producer keeps every length in registers and hands out
     live items only; larger batches enumerate every partition.  Both must give
-    the oracle's outputs and identical bits under static and dynamic scheduling."""
+    the oracle's outputs and identical bits under static and dynamic scheduling,
+    with empty partitions stored or skipped (a skipped item moves the CTA on to
+    its next item)."""
     gen = np.random.default_rng(rows)
     lengths = gen.integers(0, 600, size=rows)
     lengths[::7] = 0
@@ -242,7 +244,7 @@ def test_batches_past_the_register_schedule(kernel, rows):
     q, k, v, table, lens = device_case(case)
     counters = torch.zeros(2, dtype=torch.int32, device="cuda")
     outs = []
-    for flags in (0, ops.FLAG_DYNAMIC):
+    for flags in (0, ops.FLAG_DYNAMIC, ops.FLAG_SKIP_EMPTY, ops.FLAG_DYNAMIC | ops.FLAG_SKIP_EMPTY):
         out = torch.empty(rows, 4, 64, dtype=torch.bfloat16, device="cuda")
         partial = torch.full((rows, 4, 3, 64), float("nan"), device="cuda")
         lse = torch.full((rows, 4, 3), float("nan"), device="cuda")
@@ -252,16 +254,22 @@ def test_batches_past_the_register_schedule(kernel, rows):
         ops.paged_decode(args, q.device)
         outs.append((out, partial, lse))
     torch.cuda.synchronize()
-    assert torch.equal(outs[0][0], outs[1][0])
-    assert torch.equal(outs[0][2], outs[1][2])
     assert not counters.any() and ops.read_fault() == 0
+    empty = torch.tensor([[p * 256 >= n for p in range(3)] for n in lengths], device="cuda")
+    empty = empty[:, None, :].expand(rows, 4, 3)
+    assert torch.equal(outs[0][2], outs[1][2])
+    for out, partial, lse in outs[1:]:
+        assert torch.equal(outs[0][0], out)
+        assert torch.equal(outs[0][2][~empty], lse[~empty])
+        assert torch.equal(outs[0][1][~empty], partial[~empty])
+    for out, partial, lse in outs[2:]:
+        assert torch.isnan(lse[empty]).all()  # skipped: never written
     few = list(range(0, rows, max(1, rows // 12)))
     want = oracle.dense_reference(case.q[few], case.k, case.v, case.table[few],
                                   case.lengths[few], scale=0.125)
     assert_out_close(outs[1][0][few], want)
     assert torch.count_nonzero(outs[1][0][lens == 0]) == 0
-    empty = torch.tensor([[p * 256 >= n for p in range(3)] for n in lengths], device="cuda")
-    assert torch.isneginf(outs[1][2][empty[:, None, :].expand(rows, 4, 3)]).all()
+    assert torch.isneginf(outs[1][2][empty]).all()
 
 
 @pytest.mark.parametrize("kernel", KERNELS)
