@@ -85,20 +85,24 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// View of a paged pool [pages, 256, Hkv, D] as a 4-D tensor (D, Hkv, 256,
-// pages) with boxes of (64 columns, 1 head, box_tokens slots, 1 page): one
-// box is one 128-byte column band of box_tokens consecutive slots of one KV
-// head inside one page, landed with the 128-byte swizzle.
+// View of a paged pool [pages, 256, Hkv, D] as a 5-D tensor
+// (64 columns, 256 slots, D/64 column bands, Hkv, pages) with strides
+// (2 B, Hkv*D*2, 128 B, D*2, 256*Hkv*D*2) and boxes of (64, box_tokens,
+// D/64, 1, 1): one box is a whole T-token tile of one KV head inside one
+// page, landed band after band -- [band][slot][128 bytes] with the 128-byte
+// swizzle, the layout the kernels read -- so a tile of K (or V) is one copy
+// instead of D/64.  Every coordinate stays inside its extent, so every byte
+// read lies inside the pool.
 int encode_pool_map(CUtensorMap *map, const void *base, int64_t pages, int hkv, int dim,
                     int box_tokens) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return fail(PDL_ERR_CUDA, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled");
-  const cuuint64_t dims[4] = {(cuuint64_t)dim, (cuuint64_t)hkv, 256u, (cuuint64_t)pages};
-  const cuuint64_t strides[3] = {(cuuint64_t)dim * 2, (cuuint64_t)hkv * dim * 2,
+  const cuuint64_t dims[5] = {64u, 256u, (cuuint64_t)dim / 64, (cuuint64_t)hkv, (cuuint64_t)pages};
+  const cuuint64_t strides[4] = {(cuuint64_t)hkv * dim * 2, 128u, (cuuint64_t)dim * 2,
                                  (cuuint64_t)256 * hkv * dim * 2};
-  const cuuint32_t box[4] = {64u, 1u, (cuuint32_t)box_tokens, 1u};
-  const cuuint32_t elem[4] = {1u, 1u, 1u, 1u};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims,
+  const cuuint32_t box[5] = {64u, (cuuint32_t)box_tokens, (cuuint32_t)dim / 64, 1u, 1u};
+  const cuuint32_t elem[5] = {1u, 1u, 1u, 1u, 1u};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void *>(base), dims,
                         strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -1,5 +1,5 @@
 // pdl_device.cuh -- device helpers shared by the sm_100a decode kernels:
-// mbarrier pipeline primitives with bounded waits, 4-D TMA tile loads,
+// mbarrier pipeline primitives with bounded waits, 5-D TMA tile loads,
 // BF16 unpacking and the fault word.
 #pragma once
 
@@ -127,14 +127,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
-// 4-D tiled TMA load (no multicast) into CTA shared memory; completion is
+// 5-D tiled TMA load (no multicast) into CTA shared memory; completion is
 // signalled on `bar` as transaction bytes.  Coordinates are innermost first.
-__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, int c3, uint64_t *bar, uint64_t policy) {
+__device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, int c4, uint64_t *bar,
+                                            uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
       "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }

@@ -2,7 +2,7 @@
 //
 // One warp per (row, query head, column slice of at most 128 floats); lane l
 // owns 4 (or D/32 for D = 64) contiguous FP32 columns of the slice.  The
-// rows of up to min(splits, 32) partitions are copied into shared memory
+// rows of up to min(splits, 48) partitions are copied into shared memory
 // asynchronously (one 16- or 8-byte cp.async per lane and partition) while
 // the weights are loaded and reduced, so a merge costs about one memory
 // round trip.  The kernel is launched with
@@ -27,6 +27,11 @@ namespace pdl {
 namespace {
 
 constexpr int MERGE_WARPS = 4;
+// Partitions staged per round trip: rows of up to 48 live partitions arrive
+// in one (config 3 at B = 1 has 33 at ctx 2064).  At 96 KB a CTA still fits
+// beside one partition CTA of about 113 KB on an SM, so the merge CTAs are
+// scheduled, and read the lengths, while the partition kernel runs.
+constexpr int kMergeStageParts = 48;
 
 template <int D>
 __global__ void __launch_bounds__(32 * MERGE_WARPS)
@@ -60,7 +65,7 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   const float *r_src = (lse_protocol ? p.partial : p.accums) + (int64_t)row * p.row_stride + col0;
   const float *l_src = lse_protocol ? nullptr : p.denoms + (int64_t)row * p.w_row_stride;
   extern __shared__ __align__(16) float merge_stage[];
-  const int cap = min(p.splits, 32);
+  const int cap = min(p.splits, kMergeStageParts);
   float acc[E], shift, tot;
   merge_slice<E>(lse_protocol, w_src, p.w_part_stride, l_src, r_src, p.part_stride, live,
                         lane, merge_stage + (threadIdx.x >> 5) * cap * 32 * E, cap, acc, shift,
@@ -81,9 +86,9 @@ template <int D>
 cudaError_t launch_merge_t(const MergeParams &params, cudaStream_t stream) {
   constexpr int CW = D < 128 ? D : 128;
   constexpr int SLICES = D / CW;
-  // Up to 32 staged partition rows of CW floats per warp.
-  constexpr int max_smem = MERGE_WARPS * 32 * CW * 4;
-  const int smem = MERGE_WARPS * (params.splits < 32 ? params.splits : 32) * CW * 4;
+  // Up to kMergeStageParts staged partition rows of CW floats per warp.
+  constexpr int max_smem = MERGE_WARPS * kMergeStageParts * CW * 4;
+  const int smem = MERGE_WARPS * min(params.splits, kMergeStageParts) * CW * 4;
   static bool configured[kMaxDevices] = {false};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);

@@ -47,13 +47,14 @@ __device__ __forceinline__ float warp_sum_all(float v) {
 // ---------------------------------------------------------------------------
 // The partition rows are staged through shared memory: every lane issues one
 // asynchronous copy (cp.async, L2 only) per partition for up to `cap`
-// partitions before the weights are even reduced, so the rows arrive in one
-// round trip that overlaps the weights'.  `stage` is this warp's
+// partitions right after the weights are requested, so the rows arrive in
+// one round trip that overlaps the weights'.  `stage` is this warp's
 // cap * 32 * E floats of shared memory.
 template <int E>
 __device__ __forceinline__ void stage_rows(float *stage, const float *r_src, int64_t part_stride,
                                            int first, int n, int lane) {
   const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(stage + lane * E));
+#pragma unroll 4
   for (int j = 0; j < n; ++j) {
     const float *src = r_src + (int64_t)(first + j) * part_stride + lane * E;
     const uint32_t dst = dst0 + j * 32 * E * 4;
@@ -75,19 +76,22 @@ __device__ __forceinline__ void wait_staged_rows() {
 // Merges `live` partitions into acc (already scaled).  `shift` is the
 // exponent subtracted from every weight (the LSE protocol's logsum), `tot`
 // the weight total, so the merged LSE is (tot > 0 ? shift : -inf).  Rows are
-// staged `cap` (<= 32) partitions at a time.
+// staged `cap` partitions at a time (one round trip when live <= cap).
 template <int E>
 __device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_src,
                                                    int64_t w_part_stride, const float *l_src,
                                                    const float *r_src, int64_t part_stride,
                                                    int live, int lane, float *stage, int cap,
                                                    float (&acc)[E], float &shift, float &tot) {
-  stage_rows<E>(stage, r_src, part_stride, 0, min(live, cap), lane);
+  // The weights are requested first: the copies' asm statements are ordered
+  // memory operations, so loads issued after them would wait behind their
+  // issue instead of overlapping it.
   constexpr int WR = 4;
   float wreg[WR];
 #pragma unroll
   for (int i = 0; i < WR; ++i)
     wreg[i] = lane + 32 * i < live ? __ldcg(w_src + (lane + 32 * i) * w_part_stride) : -INFINITY;
+  stage_rows<E>(stage, r_src, part_stride, 0, min(live, cap), lane);
   float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < WR; ++i) mx = fmaxf(mx, wreg[i]);
@@ -113,6 +117,8 @@ __device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_sr
 
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  int staged0 = 0;      // first partition held by the stage (chunks of cap partitions)
+  bool waited = false;  // the current chunk has landed
   for (int s0 = 0; s0 < live; s0 += 32) {
     const int n = min(32, live - s0);
     const int wi = s0 / 32;
@@ -122,19 +128,42 @@ __device__ __forceinline__ void merge_slice(bool lse_protocol, const float *w_sr
                      : (s0 + lane < live ? __ldcg(w_src + (s0 + lane) * w_part_stride)
                                          : -INFINITY);
     const float wl = (s0 + lane < live) ? expf(wsrc - shift) : 0.f;
-    for (int c0 = 0; c0 < n; c0 += cap) {
-      const int m = min(cap, n - c0);
-      if (s0 + c0 > 0) {
-        __syncwarp();  // every lane is done with the previous rows
-        stage_rows<E>(stage, r_src, part_stride, s0 + c0, m, lane);
+    for (int c = 0; c < n;) {
+      const int s = s0 + c;
+      if (s >= staged0 + cap) {
+        __syncwarp();  // every lane is done with the previous chunk
+        staged0 = s;
+        stage_rows<E>(stage, r_src, part_stride, s, min(cap, live - s), lane);
+        waited = false;
       }
-      wait_staged_rows();
-      for (int j = 0; j < m; ++j) {
-        const float wk = __shfl_sync(FULL_MASK, wl, c0 + j);
-        const float *row = stage + j * 32 * E + lane * E;
+      if (!waited) {
+        wait_staged_rows();
+        waited = true;
+      }
+      const int m = min(n - c, staged0 + cap - s);
+      const float *rows = stage + (s - staged0) * 32 * E + lane * E;
+      // Partition order, 8 rows per step: their weights and rows are read
+      // before their multiply-adds, so only the adds form a dependent chain.
+      int j = 0;
+      for (; j + 8 <= m; j += 8) {
+        float wk[8], rv[8][E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, row[e], acc[e]);
+        for (int u = 0; u < 8; ++u) {
+          wk[u] = __shfl_sync(FULL_MASK, wl, c + j + u);
+#pragma unroll
+          for (int e = 0; e < E; ++e) rv[u][e] = rows[(j + u) * 32 * E + e];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = fmaf(wk[u], rv[u][e], acc[e]);
       }
+      for (; j < m; ++j) {
+        const float wk = __shfl_sync(FULL_MASK, wl, c + j);
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] = fmaf(wk, rows[j * 32 * E + e], acc[e]);
+      }
+      c += m;
     }
   }
 #pragma unroll

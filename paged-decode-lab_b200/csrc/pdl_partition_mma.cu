@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     item_heads<GC>(p, w.hs, h0, rows);
     if (w.kind == ITEM_FILL) {
       store_fill<D>(p, w, h0, rows, tid, NC * 32);
+      if (w.last) break;
       continue;
     }
     // q of head (nt*8 + grp) as B fragments for this warp's slices of D
@@ -389,11 +390,13 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float *dst = comb_acc + (tg * GC + nt * 8 + quad * 2 + j) * D + dh * KSW * 16 + grp;
+        const int g = nt * 8 + quad * 2 + j;
+        float *dst = comb_acc + (tg * GC + g) * D;
+        const int c0 = dh * KSW * 16 + grp;
 #pragma unroll
         for (int dm = 0; dm < KSW; ++dm) {
-          dst[dm * 16] = acc[nt][dm][j];
-          dst[dm * 16 + 8] = acc[nt][dm][j + 2];
+          dst[comb_col(g, c0 + dm * 16)] = acc[nt][dm][j];
+          dst[comb_col(g, c0 + dm * 16 + 8)] = acc[nt][dm][j + 2];
         }
         if (grp == 0 && dh == 0) {
           comb_ml[tg * 2 * GC + nt * 8 + quad * 2 + j] = m[nt][j];
@@ -418,6 +421,7 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
       }
     }
     combine_and_store<D, GC, NG, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
+    if (w.last) break;
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
   }
 }

@@ -4,7 +4,7 @@
 // is persistent: it walks items blockIdx.x, +gridDim.x, ... and keeps one
 // TMA pipeline running across item boundaries.
 //
-//   warp 0      producer (run_producer): live block-table entries -> 4-D TMA
+//   warp 0      producer (run_producer): live block-table entries -> 5-D TMA
 //               loads of T-token K and V tiles of one KV head into a 3-stage
 //               shared-memory ring (128-byte swizzle, L2 evict-first).
 //   warps 1..4  consumers: each owns T/4 rows of every tile.  D/8 lanes share
@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     item_heads<GC>(p, w.hs, h0, rows);
     if (w.kind == ITEM_FILL) {
       store_fill<D>(p, w, h0, rows, tid, NC * 32);
+      if (w.last) break;
       continue;
     }
     // q chunk j of every head of the sub-group, as FP32 pairs.
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     if (tg == 0) {
 #pragma unroll
       for (int g = 0; g < GC; ++g) {
-        float4 *dst = reinterpret_cast<float4 *>(mine + g * D + j * 8);
+        float4 *dst = reinterpret_cast<float4 *>(mine + g * D + comb_col(g, j * 8));
         dst[0] = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
         dst[1] = make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
       }
@@ -263,6 +264,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
     }
     combine_and_store<D, GC, NC>(p, w, h0, rows, comb_acc, comb_ml, tid);
+    if (w.last) break;
     named_barrier(1, NC * 32);  // the combine area is rewritten by the next item
   }
 }

@@ -23,12 +23,13 @@ enum ItemKind : int { ITEM_STOP = 0, ITEM_COMPUTE = 1, ITEM_FILL = 2 };
 
 struct WorkItem {
   int kind, b, split, split_end, hs, start, stop;
+  int last;  // the CTA's last item: its consumers exit after it without another hand-off
 };
 
 __device__ __forceinline__ WorkItem stop_item() {
   WorkItem w;
   w.kind = ITEM_STOP;
-  w.b = w.split = w.split_end = w.hs = w.start = w.stop = 0;
+  w.b = w.split = w.split_end = w.hs = w.start = w.stop = w.last = 0;
   return w;
 }
 
@@ -351,6 +352,7 @@ __device__ __forceinline__ bool publish(const ItemRing &r, uint32_t &k, const Wo
       d[4] = w.hs;
       d[5] = w.start;
       d[6] = w.stop;
+      d[7] = w.last;
       mbar_arrive(&r.full[s]);
     }
   }
@@ -379,6 +381,7 @@ __device__ __forceinline__ WorkItem consumer_next(const ItemRing &r, uint32_t &k
     w.hs = src[4];
     w.start = src[5];
     w.stop = src[6];
+    w.last = src[7];
   }
   named_barrier(1, NC * 32);  // every warp has read the slot before it is released
   if (leader) mbar_arrive(&r.empty[s]);
@@ -412,7 +415,7 @@ __device__ __forceinline__ WorkItem peeked_item(const ItemRing &r, uint32_t k) {
 // (static) every gridDim.x-th item -- publishes each to the consumers and,
 // for compute items, reads the partition's block-table entries (32 per load,
 // one per lane, never past the table width) and issues one T-token tile of K
-// and V per stage as D/64 TMA boxes each.  T divides 256, so a tile never
+// and V per stage, one TMA box each.  T divides 256, so a tile never
 // spans two pages.  The next item is claimed once this one's first copies
 // are issued, so the atomic's round trip overlaps them.
 template <int D, int T, int NS>
@@ -420,8 +423,6 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
                              const PartitionParams &p, uint8_t *kbuf, uint8_t *vbuf,
                              uint64_t *full, uint64_t *empty, volatile int *abort_flag,
                              const ItemRing &ring, int lane) {
-  constexpr int SUBTILES = D / 64;
-  constexpr int SUB_BYTES = T * 128;
   constexpr int TILE_BYTES = T * D * 2;
   const uint64_t policy = l2_evict_first_policy();
   if (lane == 0) {
@@ -474,6 +475,10 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
         w = decode_dense(p, item, p.sched != nullptr, lane, skip, base, my_page);
       }
     }
+    // Dense enumeration without claims past the first wave: the next item is
+    // item + gridDim.x, so whether this one is the CTA's last is known now.
+    if (!live && (p.sched == nullptr || total <= (int)gridDim.x) && item + (int)gridDim.x >= total)
+      w.last = 1;
     // A skipped item (empty, its partition not stored) moves on to the next.
     if (w.kind == ITEM_STOP && !skip) {
       publish(ring, k, w, p.fault, abort_flag, lane);
@@ -514,13 +519,8 @@ __device__ void run_producer(const CUtensorMap *k_map, const CUtensorMap *v_map,
             ok = false;
           } else {
             mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
-#pragma unroll
-            for (int st = 0; st < SUBTILES; ++st) {
-              tma_load_4d(kbuf + s * TILE_BYTES + st * SUB_BYTES, k_map, st * 64, kvh, tok & 255,
-                          page, &full[s], policy);
-              tma_load_4d(vbuf + s * TILE_BYTES + st * SUB_BYTES, v_map, st * 64, kvh, tok & 255,
-                          page, &full[s], policy);
-            }
+            tma_load_5d(kbuf + s * TILE_BYTES, k_map, 0, tok & 255, 0, kvh, page, &full[s], policy);
+            tma_load_5d(vbuf + s * TILE_BYTES, v_map, 0, tok & 255, 0, kvh, page, &full[s], policy);
           }
         }
         ok = __shfl_sync(FULL_MASK, ok, 0);
@@ -595,15 +595,24 @@ __device__ __forceinline__ void item_heads(const PartitionParams &p, int hs, int
   rows = min(GC, p.group - sub * GC);
 }
 
+// Column of element (head g, column d) in a row of the combine area: bits 3-4
+// of the column are XOR-ed with bits 1-2 of g, so the four head rows that an
+// MMA fragment stores at once (g = quad * 2 + j) fall in four different
+// groups of 8 banks instead of the same ones; 4 consecutive columns stay
+// contiguous (float4 reads).
+__device__ __forceinline__ int comb_col(int g, int d) { return d ^ (((g >> 1) & 3) << 3); }
+
 // Merge NC per-warp (or per-group) softmax states of one item and store the
 // outputs, with the NW consumer warps' threads (tid < NW * 32).
-//   comb_acc [NC][GC][D]  unnormalised accumulators (relative to each state's max)
+//   comb_acc [NC][GC][D]  unnormalised accumulators (relative to each state's max),
+//                         columns placed by comb_col
 //   comb_ml  [NC][2][GC]  per-state running max (base-2 scaled units) and sum
 // M = max_w m_w; f_w = 2^(m_w - M); L = sum f_w l_w; O = sum f_w acc_w.
 // Stores O/L + LSE (natural log), (M ln2, L, O), or BF16 O/L.
 template <int D, int GC, int NC, int NW = NC>
 __device__ void combine_and_store(const PartitionParams &p, const WorkItem &w, int h0, int rows,
                                   const float *comb_acc, const float *comb_ml, int tid) {
+#pragma unroll 2
   for (int e = tid * 4; e < rows * D; e += NW * 32 * 4) {
     const int g = e / D, d = e % D;
     float mx = -INFINITY;
@@ -616,7 +625,7 @@ __device__ void combine_and_store(const PartitionParams &p, const WorkItem &w, i
       const float mw = comb_ml[wi * 2 * GC + g];
       const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
       den += f * comb_ml[wi * 2 * GC + GC + g];
-      const float4 a = *reinterpret_cast<const float4 *>(comb_acc + (wi * GC + g) * D + d);
+      const float4 a = *reinterpret_cast<const float4 *>(comb_acc + (wi * GC + g) * D + comb_col(g, d));
       o.x += f * a.x;
       o.y += f * a.y;
       o.z += f * a.z;
