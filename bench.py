@@ -427,8 +427,8 @@ def exchange_micro(reps=20, steps=20):
 
 
 # ---------------------------------------------------------------- multi-GPU parity
-def full_decode(w, tokens_per_split, splits, kernel, device):
-    """One-GPU decode of a whole batch with the given partition size: the
+def full_decode(w, tokens_per_split, splits, kernel, device, flags=0):
+    """One-GPU decode of a whole batch with the given partitioning: the
     parity reference of the sharded modes (same kernels and bounds per row)."""
     import torch
     from paged_decode import ops
@@ -439,7 +439,7 @@ def full_decode(w, tokens_per_split, splits, kernel, device):
     ops.paged_decode(ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
                                      tokens_per_split=tokens_per_split, splits=splits,
                                      protocol=ops.PROTOCOL_LSE, kernel=kernel, out=out,
-                                     partial=partial, lse=lse), device)
+                                     partial=partial, lse=lse, flags=flags), device)
     torch.cuda.synchronize(device)
     return out
 
@@ -455,7 +455,7 @@ def check_parity(mode, out, full, plan, shards, kernel, world, rank, device):
             from paged_decode import ops
             from paged_decode.splitkv_plan import make_b200_plan
             g = make_b200_plan(full.spec, ops.sm_count(device))
-            want = full_decode(full, g.tokens_per_split, g.splits, kernel, device)
+            want = full_decode(full, g.tokens_per_split, g.splits, kernel, device)  # fixed bounds
             err = float((out.float() - want.float()).abs().max().item())
             ok = err <= 2.0 ** -7 and bool(torch.isfinite(out.float()).all().item())
         reference = "one-GPU decode of the global batch (B200 plan), max-abs 2^-7"
@@ -464,7 +464,9 @@ def check_parity(mode, out, full, plan, shards, kernel, world, rank, device):
         dist.all_gather_into_tensor(gathered, out.contiguous())
         if rank == 0:
             got = torch.cat(list(gathered), dim=1)
-            want = full_decode(full, plan.tokens_per_split, plan.splits, kernel, device)
+            from paged_decode.splitkv_plan import launch_partitioning
+            tokens, bounds = launch_partitioning(plan)
+            want = full_decode(full, tokens, plan.splits, kernel, device, flags=bounds)
             ok = torch.equal(got, want)
             err = float((got.float() - want.float()).abs().max().item())
         reference = "one-GPU decode of the global batch, same partitions: bit-exact"
@@ -479,7 +481,9 @@ def check_parity(mode, out, full, plan, shards, kernel, world, rank, device):
             got = torch.empty_like(full.q)
             for r, rows in enumerate(shards):
                 got[torch.as_tensor(rows, device=device)] = gathered[r, :len(rows)]
-            want = full_decode(full, plan.tokens_per_split, plan.splits, kernel, device)
+            from paged_decode.splitkv_plan import launch_partitioning
+            tokens, bounds = launch_partitioning(plan)
+            want = full_decode(full, tokens, plan.splits, kernel, device, flags=bounds)
             ok = torch.equal(got, want)
             err = float((got.float() - want.float()).abs().max().item())
         reference = "one-GPU decode of the global batch, same partitions: bit-exact"
@@ -640,11 +644,13 @@ def main(argv=None):
             return matched_decode(w.q, w.k, w.v, w.table, w.lengths,
                                   resources=out_slots[slot], scale=w.scale, kernel=args.kernel)
 
+        from paged_decode.splitkv_plan import launch_partitioning
+        tokens, bounds = launch_partitioning(plan)
         part_args = [ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
-                                     tokens_per_split=plan.tokens_per_split, splits=plan.splits,
+                                     tokens_per_split=tokens, splits=plan.splits,
                                      protocol=ops.PROTOCOL_LSE, kernel=args.kernel, out=res.out,
                                      partial=res.partials, lse=res.lse, counters=res.counters,
-                                     flags=ops.FLAG_DYNAMIC) for w in wls]
+                                     flags=ops.FLAG_DYNAMIC | bounds) for w in wls]
         out_buf = res.out
 
     def step(i):
@@ -842,6 +848,7 @@ def main(argv=None):
                        "num_heads": gspec.num_heads, "num_kv_heads": gspec.num_kv_heads,
                        "head_dim": gspec.head_dim, "context": gspec.max_context_len,
                        "splits": plan.splits, "tokens_per_split": plan.tokens_per_split,
+                       "balanced_partitions": bool(plan.balanced),
                        "kv_bytes_per_step": job_bytes, "kernel": kernel_name,
                        "mode": mode, "parallelism": parallelism,
                        "timing": f"{K}-step CUDA graph replayed {reps}x back to back",

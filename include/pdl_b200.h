@@ -30,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st *pdl_stream_t; /* same handle as cudaStream_t */
 
-#define PDL_ABI_VERSION 4
+#define PDL_ABI_VERSION 5
 #define PDL_PAGE_SIZE 256
 
 typedef enum PdlStatus {
@@ -82,7 +82,16 @@ typedef enum PdlFlags {
    * counters[0] and counters[1] (zero-initialised once; the kernel leaves
    * them zeroed).  The counter is touched only when a launch has more live
    * work items than CTAs.  Outputs are bit-identical to static scheduling. */
-  PDL_FLAG_DYNAMIC = 8
+  PDL_FLAG_DYNAMIC = 8,
+  /* Partition bounds follow each row's length (no counterpart in the
+   * reference, whose partitions are fixed tokens_per_split ranges): with
+   * L = min(max(len, 0), table_width * 256) and G = tokens_per_split (> 0,
+   * the granule), partition p of the row covers [p*c, min((p+1)*c, L)) with
+   * c = G * ceil(ceil(L / splits) / G), so a row's live partitions are equal
+   * up to the last one; ceil(L / c) of them are live.  The merge derives the
+   * same bounds.  For single-wave launches whose rows are shorter than the
+   * table capacity the split plan was made for (pdl_b200_plan sets it). */
+  PDL_FLAG_BALANCED = 16
 } PdlFlags;
 
 /* Geometry contract; mirrors DecodeSpec (reference src/paged_decode/spec.py:11-30). */
@@ -104,6 +113,10 @@ typedef struct PdlPlan {
   int32_t lse_lanes;
   int32_t sm_count;
   int32_t explicit_splits;  /* 1: policy "explicit", 0: "pinned_geometry" */
+  int32_t balanced;         /* pdl_b200_plan only: 1 when the plan recommends launching
+                               with PDL_FLAG_BALANCED and tokens_per_split = tile_tokens
+                               (the granule); tokens_per_split above stays the fixed-bounds
+                               plan.  0 in reference plans. */
 } PdlPlan;
 
 /* Arguments of one decode launch.  Element strides, not bytes. */

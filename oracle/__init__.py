@@ -21,5 +21,6 @@ from .reference import (  # noqa: F401
     validate_metadata, gather_kv, dense_reference, partial, merge_partials,
     streaming_reference, partition_bounds, normalized_partitions, lse_merge,
     unnormalized_partitions, merge_unnormalized, matched_reference, score_magnitudes,
+    balanced_span,
 )
 from .plan import OraclePlan, make_splitkv_plan, spec_geometry  # noqa: F401

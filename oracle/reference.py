@@ -165,21 +165,33 @@ def streaming_reference(q, k, v, table, lengths, split=False, scale=None,
 # --------------------------------------------------------------------------
 # Split-KV protocols of the GPU kernels
 # --------------------------------------------------------------------------
-def partition_bounds(length, tokens_per_split, splits):
+def balanced_span(length, splits, granule):
+    """Tokens per partition of a row split into ``splits`` partitions that
+    follow its length, in whole granules: G * ceil(ceil(L / S) / G).  This
+    library's PDL_FLAG_BALANCED; no counterpart in the reference."""
+    per = -(-int(length) // splits)
+    return -(-per // granule) * granule
+
+
+def partition_bounds(length, tokens_per_split, splits, balanced=False):
     """[start, end) of each partition (matched_splitkv.py:75-76, kernels.py:58-60).
 
     Partition p covers [p*T, min((p+1)*T, length)); it is empty when
-    p*T >= length.  Integer arithmetic -- the GPU must match it bit-exactly.
+    p*T >= length.  With ``balanced`` (no reference counterpart), T is
+    balanced_span(length, splits, tokens_per_split) instead.  Integer
+    arithmetic -- the GPU must match it bit-exactly.
     """
+    span = balanced_span(length, splits, tokens_per_split) if balanced else tokens_per_split
     bounds = []
     for p in range(splits):
-        start = p * tokens_per_split
-        end = min(start + tokens_per_split, int(length))
+        start = p * span
+        end = min(start + span, int(length))
         bounds.append((start, max(start, end)))
     return bounds
 
 
-def normalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, scale=None):
+def normalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, scale=None,
+                          balanced=False):
     """Normalised partial + LSE per partition (matched_splitkv.py:52-98).
 
     partial = acc / l and lse = m + ln(l) with m in scaled-score units
@@ -195,7 +207,7 @@ def normalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, sca
     for b in range(batch):
         n = int(lengths[b])
         keys, vals = gather_kv(k, table[b], n), gather_kv(v, table[b], n)
-        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits)):
+        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits, balanced)):
             if end <= start:
                 continue
             for h in range(heads):
@@ -207,7 +219,8 @@ def normalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, sca
     return partials, lse
 
 
-def score_magnitudes(q, k, table, lengths, tokens_per_split, splits, scale=None):
+def score_magnitudes(q, k, table, lengths, tokens_per_split, splits, scale=None,
+                     balanced=False):
     """Per partition, the largest sum_i |q_i * k_ti| * |scale| over its tokens.
 
     This is the magnitude an FP32 dot product's rounding error scales with
@@ -224,7 +237,7 @@ def score_magnitudes(q, k, table, lengths, tokens_per_split, splits, scale=None)
     for b in range(batch):
         n = int(lengths[b])
         keys = np.abs(gather_kv(k, table[b], n).astype(np.float64))
-        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits)):
+        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits, balanced)):
             if end <= start:
                 continue
             for h in range(heads):
@@ -250,7 +263,8 @@ def lse_merge(partials, lse):
     return (weights[..., None] * partials).sum(axis=-2).astype(np.float32)
 
 
-def unnormalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, scale=None):
+def unnormalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, scale=None,
+                            balanced=False):
     """(m, l, acc) per partition as stored by the split kernel (kernels.py:44-80).
 
     m is in scaled-score units, -inf with l = 0 and acc = 0 for empty
@@ -266,7 +280,7 @@ def unnormalized_partitions(q, k, v, table, lengths, tokens_per_split, splits, s
     for b in range(batch):
         n = int(lengths[b])
         keys, vals = gather_kv(k, table[b], n), gather_kv(v, table[b], n)
-        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits)):
+        for p, (start, end) in enumerate(partition_bounds(n, tokens_per_split, splits, balanced)):
             if end <= start:
                 continue
             for h in range(heads):
@@ -290,11 +304,12 @@ def merge_unnormalized(maxima, denoms, accums):
     return (num / np.where(total > 0, total, 1)[..., None]).astype(np.float32)
 
 
-def matched_reference(q, k, v, table, lengths, tokens_per_split, splits, scale=None):
+def matched_reference(q, k, v, table, lengths, tokens_per_split, splits, scale=None,
+                      balanced=False):
     """Partition + LSE merge, the two-kernel path of matched_splitkv.py:130-150.
 
     Returns (out [B,Hq,D], partials [B,Hq,S,D], lse [B,Hq,S]).
     """
     partials, lse = normalized_partitions(q, k, v, table, lengths, tokens_per_split,
-                                          splits, scale)
+                                          splits, scale, balanced)
     return lse_merge(partials, lse), partials, lse

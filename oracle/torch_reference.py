@@ -7,6 +7,8 @@ of the split-K kernels it checks.  Rows of length 0 give zeros.
 """
 import torch
 
+from .reference import balanced_span
+
 
 def dense_reference(q, k, v, tables, lengths, scale=None):
     scale = q.shape[-1] ** -0.5 if scale is None else scale
@@ -75,10 +77,12 @@ def chunked_reference_rows(q, k, v, tables, lengths, rows, scale=None, chunk=655
     return out
 
 
-def chunked_partition_lse(q, k, tables, lengths, rows, tokens_per_split, splits, scale=None):
+def chunked_partition_lse(q, k, tables, lengths, rows, tokens_per_split, splits, scale=None,
+                          balanced=False):
     """FP64 natural-log LSE of the scaled scores of every partition
     [p * T, min((p + 1) * T, len)) of the selected rows, [len(rows), Hq, S],
-    -inf for empty partitions; and each partition's score magnitude (the
+    -inf for empty partitions (``balanced``: the partitions of
+    reference.balanced_span instead); and each partition's score magnitude (the
     largest sum_i |q_i k_i| * |scale| over its tokens, 0 when empty), the
     scale an FP32 score's rounding error grows with.  Evaluated on the GPU,
     one partition of one KV head at a time."""
@@ -91,8 +95,9 @@ def chunked_partition_lse(q, k, tables, lengths, rows, tokens_per_split, splits,
     lens = lengths.cpu().tolist()
     for i, b in enumerate(rows):
         n = lens[b]
+        span = balanced_span(n, splits, tokens_per_split) if balanced else tokens_per_split
         for p in range(splits):
-            lo, hi = p * tokens_per_split, min(n, (p + 1) * tokens_per_split)
+            lo, hi = p * span, min(n, (p + 1) * span)
             if hi <= lo:
                 continue
             t = torch.arange(lo, hi, device=q.device)

@@ -178,8 +178,11 @@ int validate_common(const PdlDecodeArgs *a) {
   if (a->splits <= 0 || a->tokens_per_split < 0) return PDL_ERR_SPLITS;
   if (a->tokens_per_split == 0 && a->splits != 1) return PDL_ERR_SPLITS;
   if (a->protocol != PDL_PROTOCOL_LSE && a->protocol != PDL_PROTOCOL_MLA) return PDL_ERR_SHAPE;
-  if (a->flags & ~(PDL_FLAG_SKIP_EMPTY | PDL_FLAG_DIRECT_SINGLE | PDL_FLAG_DYNAMIC))
+  if (a->flags & ~(PDL_FLAG_SKIP_EMPTY | PDL_FLAG_DIRECT_SINGLE | PDL_FLAG_DYNAMIC |
+                   PDL_FLAG_BALANCED))
     return fail(PDL_ERR_SHAPE, "flags", "unknown PdlFlags bit");
+  if ((a->flags & PDL_FLAG_BALANCED) && a->tokens_per_split == 0)
+    return fail(PDL_ERR_SPLITS, "flags", "balanced partitions need a granule (tokens_per_split)");
   return PDL_OK;
 }
 
@@ -191,8 +194,9 @@ int validate_partition_inputs(const PdlDecodeArgs *a) {
   if (a->q_stride_head < a->head_dim || a->q_stride_batch < 1) return PDL_ERR_SHAPE;
   if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)) return PDL_ERR_ALIGNMENT;
   if (!aligned(a->q, 2)) return PDL_ERR_ALIGNMENT;
-  if (a->tokens_per_split > 0) {
-    // Every token the table can address must belong to some partition.
+  if (a->tokens_per_split > 0 && !(a->flags & PDL_FLAG_BALANCED)) {
+    // Every token the table can address must belong to some partition
+    // (balanced partitions always cover the row).
     const int64_t covered = (int64_t)a->splits * a->tokens_per_split;
     if (covered < (int64_t)a->table_width * PDL_PAGE_SIZE) return PDL_ERR_SPLITS;
   }
@@ -291,6 +295,7 @@ int run_partition(const PdlDecodeArgs *a, int mode, cudaStream_t stream) {
   // finished CTAs.  The kernel uses them only when a launch has more live
   // items than CTAs (each CTA's first item is blockIdx.x, no atomic).
   p.sched = (a->flags & PDL_FLAG_DYNAMIC) ? a->counters : nullptr;
+  p.balanced = (a->flags & PDL_FLAG_BALANCED) ? 1 : 0;
   const cudaError_t e = which == PDL_KERNEL_SIMT ? launch_partition_simt(L, stream)
                                                  : launch_partition_mma(L, stream);
   return status_from_cuda(e, which == PDL_KERNEL_SIMT ? "partition (simt)" : "partition (mma)");
@@ -312,6 +317,8 @@ int run_merge(const PdlDecodeArgs *a, cudaStream_t stream, bool after_partition)
   // 0, so the merge reads only the live ones whenever lengths are known.
   m.lengths = a->lengths;
   m.early_lengths = after_partition ? 1 : 0;
+  m.balanced = (a->flags & PDL_FLAG_BALANCED) ? 1 : 0;
+  m.cap_tokens = a->table_width * PDL_PAGE_SIZE;
   m.num_heads = a->num_heads;
   m.tokens_per_split = a->tokens_per_split > 0 ? a->tokens_per_split : (1 << 30);
   m.rows = a->batch * a->num_heads;
@@ -424,6 +431,7 @@ extern "C" int pdl_splitkv_plan(const PdlSpec *spec, int32_t sm_count, int32_t n
   plan->lse_lanes = (int32_t)std::min<int64_t>(padded, 128 / merge_rows);
   plan->sm_count = sm_count;
   plan->explicit_splits = num_splits ? 1 : 0;
+  plan->balanced = 0;
   return PDL_OK;
 }
 
@@ -457,6 +465,12 @@ extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *pla
   splits = std::min<int64_t>(std::max<int64_t>(splits, 1), blocks);
   const int64_t tps = (blocks + splits - 1) / splits * tile;
   splits = (capacity + tps - 1) / tps;  // drop partitions that would always be empty
+  // One wave of long D = 256 items: the plan is made from the table capacity,
+  // but rows are often shorter (config 3: 2064 of 2560 tokens splits into
+  // 1280 + 784 with fixed bounds), so the plan recommends partitions that
+  // follow each row's length (PDL_FLAG_BALANCED, granule tile_tokens).
+  const bool balanced = spec->head_dim == 256 && splits > 1 && groups * splits <= slots &&
+                        tps > 4 * tile;
   int64_t padded = 1;
   while (padded < splits) padded <<= 1;
   plan->splits = (int32_t)splits;
@@ -466,6 +480,7 @@ extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *pla
   plan->lse_lanes = (int32_t)std::min<int64_t>(padded, 32);
   plan->sm_count = sm_count;
   plan->explicit_splits = 1;
+  plan->balanced = balanced ? 1 : 0;
   return PDL_OK;
 }
 

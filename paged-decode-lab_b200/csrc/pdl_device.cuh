@@ -127,6 +127,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
+// Tokens per partition of a row of (clamped) length len split into `splits`
+// balanced partitions of whole granules: granule * ceil(ceil(len / splits) /
+// granule); 0 for an empty row.  Partition p covers [p * span, (p + 1) *
+// span) of the row; the partition and merge kernels both use this.
+__host__ __device__ __forceinline__ int balanced_span(int len, int splits, int granule) {
+  const int per = (len + splits - 1) / splits;
+  return (per + granule - 1) / granule * granule;
+}
+
 // 5-D tiled TMA load (no multicast) into CTA shared memory; completion is
 // signalled on `bar` as transaction bytes.  Coordinates are innermost first.
 __device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, int c0, int c1,

@@ -52,6 +52,8 @@ struct PartitionParams {
   int32_t *sched;           // dynamic scheduling: [items claimed, finished CTAs], or null (static)
   int32_t live;             // enumerate live items only (set by the launcher: multi-wave
                             // launches of batches up to 512 rows)
+  int32_t balanced;         // partition bounds from each row's length (balanced_span);
+                            // tokens_per_split is then the granule
 };
 
 // Partition p of row r: rows at partial/accums[r*row_stride + p*part_stride],
@@ -72,6 +74,9 @@ struct MergeParams {
   const int32_t *lengths;   // optional: bound the partitions read per row
   int32_t early_lengths;    // launched right after the partition kernel: read lengths
                             // before the dependency wait
+  int32_t balanced;         // partitions follow the row lengths (balanced_span)
+  int32_t cap_tokens;       // table_width * 256: lengths are clamped to it like the
+                            // partition kernel clamps them
   int32_t num_heads;
   int32_t tokens_per_split;
   int32_t rows;             // batch * num_heads

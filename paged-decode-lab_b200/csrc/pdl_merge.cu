@@ -20,7 +20,8 @@
 // feed another merge.
 // When `lengths` is given, only the ceil(len / tokens_per_split) live
 // partitions of a row are read (the others hold no tokens and their weights
-// are exactly 0), so empty partitions need not be stored at all.
+// are exactly 0), so empty partitions need not be stored at all; with
+// balanced partitions, ceil(len / balanced_span(len)).
 #include "pdl_merge_core.cuh"
 
 namespace pdl {
@@ -58,7 +59,13 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
   int live = p.splits;
   if (p.lengths != nullptr) {
     if (!p.early_lengths) len = __ldg(p.lengths + row / p.num_heads);
-    live = min(live, (int)((max(len, 0) + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+    if (p.balanced) {
+      const int clamped = min(max(len, 0), p.cap_tokens);
+      const int span = balanced_span(clamped, p.splits, p.tokens_per_split);
+      live = span > 0 ? min(live, (clamped + span - 1) / span) : 0;
+    } else {
+      live = min(live, (int)((max(len, 0) + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
+    }
   }
   const bool lse_protocol = p.protocol == MODE_LSE;
   const float *w_src = (lse_protocol ? p.lse : p.maxima) + (int64_t)row * p.w_row_stride;

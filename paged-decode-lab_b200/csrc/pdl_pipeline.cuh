@@ -291,12 +291,19 @@ __device__ __forceinline__ WorkItem decode_dense(const PartitionParams &p, int i
   }
   w.b = rest / per_row;
   w.hs = rest % per_row;
-  const int64_t start = (int64_t)w.split * p.tokens_per_split;
-  base = start < (int64_t)row_capacity(p) ? (int)(start >> 8) : -64;
+  // Fixed partitions start at split * tokens_per_split; balanced ones at
+  // split * span with span >= tokens_per_split (the granule), so in both
+  // cases the table window requested with the length starts at or before
+  // the partition's first page (the tile loop moves it forward if needed).
+  const int64_t lo = (int64_t)w.split * p.tokens_per_split;
+  base = lo < (int64_t)row_capacity(p) ? (int)(lo >> 8) : -64;
   my_page = (base >= 0 && base + lane < p.table_width)
                 ? __ldg(p.table + (int64_t)w.b * p.table_stride + base + lane) : 0;
   const int len = clamp_length(p, w.b);
-  const int64_t stop = min((int64_t)len, start + p.tokens_per_split);
+  const int64_t span = p.balanced ? balanced_span(len, p.splits, p.tokens_per_split)
+                                  : p.tokens_per_split;
+  const int64_t start = (int64_t)w.split * span;
+  const int64_t stop = min((int64_t)len, start + span);
   skip = false;
   if (start < stop) {
     w.kind = ITEM_COMPUTE;
@@ -662,9 +669,10 @@ __device__ void combine_and_store(const PartitionParams &p, const WorkItem &w, i
 
 // Host: the live schedule pays when a launch has more (dense) items than CTAs
 // -- partitions past the rows' lengths would otherwise cost claims -- and the
-// lengths fit the producer's registers and local memory.
+// lengths fit the producer's registers and local memory.  Balanced partition
+// bounds are derived per item (dense enumeration only).
 inline int live_schedule(const PartitionParams &p, int grid) {
-  return p.batch <= 32 * RMAX && p.n_items > grid ? 1 : 0;
+  return !p.balanced && p.batch <= 32 * RMAX && p.n_items > grid ? 1 : 0;
 }
 
 // Dynamic shared memory one CTA may use so that two CTAs share an SM

@@ -8,7 +8,7 @@ import ctypes
 from pathlib import Path
 
 LIBRARY = Path(__file__).with_name("libpdl_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 PDL_OK = 0
 STATUS_NAMES = {
@@ -18,7 +18,7 @@ STATUS_NAMES = {
 }
 PROTOCOL_LSE, PROTOCOL_MLA = 0, 1
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_MMA = 0, 1, 2
-FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_DYNAMIC = 1, 2, 8
+FLAG_SKIP_EMPTY, FLAG_DIRECT_SINGLE, FLAG_DYNAMIC, FLAG_BALANCED = 1, 2, 8, 16
 
 # Every extern "C" symbol declared in include/pdl_b200.h.
 SYMBOLS = ("pdl_partition", "pdl_merge", "pdl_lse_merge", "pdl_paged_decode", "pdl_append_kv",
@@ -42,7 +42,7 @@ class PdlSpec(ctypes.Structure):
 class PdlPlan(ctypes.Structure):
     _fields_ = [("splits", _i32), ("tile_tokens", _i32), ("tokens_per_split", _i32),
                 ("table_capacity_tokens", _i32), ("lse_lanes", _i32), ("sm_count", _i32),
-                ("explicit_splits", _i32)]
+                ("explicit_splits", _i32), ("balanced", _i32)]
 
 
 class PdlDecodeArgs(ctypes.Structure):

@@ -14,7 +14,7 @@ import torch
 
 from . import ops
 from .runtime import _validate
-from .splitkv_plan import make_splitkv_plan
+from .splitkv_plan import launch_partitioning, make_splitkv_plan
 
 
 @dataclass
@@ -80,12 +80,13 @@ def matched_decode(q, k, v, tables, lengths, *, resources, scale=None, kernel="a
         if (tensor.shape != geometry or tensor.device != q.device
                 or tensor.dtype != torch.float32 or not tensor.is_contiguous()):
             raise ValueError("invalid matched workspace")
+    tokens, bounds = launch_partitioning(plan)
     args = ops.decode_args(q, k, v, tables, lengths, scale=scale,
-                           tokens_per_split=plan.tokens_per_split, splits=plan.splits,
+                           tokens_per_split=tokens, splits=plan.splits,
                            protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
                            partial=resources.partials, lse=resources.lse,
                            counters=resources.counters,
-                           flags=0 if resources.counters is None else ops.FLAG_DYNAMIC)
+                           flags=bounds | (0 if resources.counters is None else ops.FLAG_DYNAMIC))
     ops.paged_decode(args, q.device)
     cache.put(key, args)
     return resources.out

@@ -20,6 +20,7 @@ KERNEL_MMA = _lib.KERNEL_MMA
 FLAG_SKIP_EMPTY = _lib.FLAG_SKIP_EMPTY
 FLAG_DIRECT_SINGLE = _lib.FLAG_DIRECT_SINGLE
 FLAG_DYNAMIC = _lib.FLAG_DYNAMIC
+FLAG_BALANCED = _lib.FLAG_BALANCED
 
 _KERNELS = {"auto": KERNEL_AUTO, "simt": KERNEL_SIMT, "mma": KERNEL_MMA}
 

@@ -21,6 +21,20 @@ class SplitKVPlan:
     lse_lanes: int
     sm_count: int
     policy: str
+    # Not in the reference: the B200 plan may recommend partitions that follow
+    # each row's length (PDL_FLAG_BALANCED, granule tile_tokens); see
+    # launch_partitioning.
+    balanced: bool = False
+
+
+def launch_partitioning(plan):
+    """(tokens_per_split, flags) to launch ``plan`` with: the fixed partitions
+    of ``plan.tokens_per_split`` tokens, or -- when the plan recommends it --
+    balanced partitions of whole ``tile_tokens`` granules with
+    ``PDL_FLAG_BALANCED``."""
+    if plan.balanced:
+        return plan.tile_tokens, _lib.FLAG_BALANCED
+    return plan.tokens_per_split, 0
 
 
 def make_splitkv_plan(spec, sm_count, *, num_splits=0):
@@ -45,7 +59,9 @@ def make_b200_plan(spec, sm_count):
 
     About one work item per CTA slot (two CTAs per SM), items of at most
     4096 tokens so variable-length batches balance under dynamic scheduling,
-    partitions a multiple of the reference plan's tile.  Use it through
+    partitions a multiple of the reference plan's tile.  For one wave of long
+    D = 256 items ``balanced`` is set: launch it as ``launch_partitioning``
+    says (``matched_decode`` does).  Use it through
     ``allocate_matched_resources(spec, device, plan=make_b200_plan(spec, sms))``:
     ``num_splits=plan.splits`` would recompute ``tokens_per_split`` with the
     reference heuristic's rounding, which can give other partition bounds.
@@ -58,4 +74,5 @@ def make_b200_plan(spec, sm_count):
     if status != _lib.PDL_OK:
         raise ValueError(f"invalid plan request: {_lib.status_text(status)}")
     return SplitKVPlan(plan.splits, plan.tile_tokens, plan.tokens_per_split,
-                       plan.table_capacity_tokens, plan.lse_lanes, plan.sm_count, "b200")
+                       plan.table_capacity_tokens, plan.lse_lanes, plan.sm_count, "b200",
+                       bool(plan.balanced))

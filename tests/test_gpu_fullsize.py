@@ -12,7 +12,8 @@ at full size the checks are:
     (and rewriting the block table to match) leaves every output bit
     unchanged, and dynamic scheduling gives the bits of static scheduling.
 The split plan is the bench's: the reference plan's 2 partitions for config 2,
-this library's B200 plan otherwise.
+this library's B200 plan otherwise (launched as launch_partitioning says: config 3 at
+B=8 and 32 with partitions that follow each row's length).
 """
 import pytest
 import torch
@@ -21,7 +22,7 @@ from gpu_util import assert_lse_close, assert_out_close, requires_cuda
 from oracle.torch_reference import chunked_partition_lse, chunked_reference_rows
 from paged_decode import ops
 from paged_decode.matched_splitkv import allocate_matched_resources, matched_decode
-from paged_decode.splitkv_plan import make_b200_plan, make_splitkv_plan
+from paged_decode.splitkv_plan import launch_partitioning, make_b200_plan, make_splitkv_plan
 from paged_decode.workloads import make_workload
 
 pytestmark = [pytest.mark.gpu, requires_cuda]
@@ -69,8 +70,9 @@ def test_full_size_rows_and_partition_lse_match_fp64_reference(name, batch, cont
     want = chunked_reference_rows(w.q, w.k, w.v, w.table, w.lengths, rows, scale=w.scale)
     assert_out_close(out[rows], want.float(), what=f"{name} rows {rows}")
     assert torch.isfinite(out.float()).all()
-    lse, mag = chunked_partition_lse(w.q, w.k, w.table, w.lengths, rows, plan.tokens_per_split,
-                                     plan.splits, scale=w.scale)
+    tokens, bounds = launch_partitioning(plan)
+    lse, mag = chunked_partition_lse(w.q, w.k, w.table, w.lengths, rows, tokens, plan.splits,
+                                     scale=w.scale, balanced=bool(bounds))
     assert_lse_close(res.lse[rows], lse.cpu().numpy(), what=f"{name} lse rows {rows}",
                      score_mag=mag.cpu().numpy())
 
@@ -100,8 +102,9 @@ def test_full_size_page_relocation_and_scheduling_are_bit_exact(name):
     # Static round-robin scheduling (no counters) against the dynamic default.
     out = torch.empty_like(res.out)
     partial, lse = torch.empty_like(res.partials), torch.empty_like(res.lse)
+    tokens, bounds = launch_partitioning(plan)
     args = ops.decode_args(w.q, w.k, w.v, w.table, w.lengths, scale=w.scale,
-                           tokens_per_split=plan.tokens_per_split, splits=plan.splits,
+                           tokens_per_split=tokens, splits=plan.splits, flags=bounds,
                            protocol=ops.PROTOCOL_LSE, out=out, partial=partial, lse=lse)
     ops.paged_decode(args, DEV)
     assert torch.equal(out, base)

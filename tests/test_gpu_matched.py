@@ -298,3 +298,97 @@ def test_dynamic_scheduling_is_bit_identical_to_static(kernel):
     sub = oracle.dense_reference(case.q[few], case.k, case.v, case.table[few], case.lengths[few],
                                  scale=0.088)
     assert_out_close(outs[1][few], sub)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("protocol", ["lse", "mla"])
+@pytest.mark.parametrize("flags", [0, "dynamic+skip"])
+@pytest.mark.parametrize("hq,hkv,d,granule,splits", [(16, 4, 256, 64, 3), (8, 2, 128, 64, 5),
+                                                     (4, 1, 64, 128, 2), (8, 2, 256, 32, 40)])
+def test_balanced_partitions_follow_each_rows_length(kernel, protocol, flags, hq, hkv, d,
+                                                     granule, splits):
+    """PDL_FLAG_BALANCED: partition p of a row covers [p*c, (p+1)*c) with
+    c = granule * ceil(ceil(len / splits) / granule).  Live partitions hold
+    the oracle's values for exactly those bounds, the others are stored empty
+    (or untouched with PDL_FLAG_SKIP_EMPTY), and the merge, which derives
+    the same bounds, gives the dense softmax."""
+    lengths = [3000, 0, 1, 4096, 257, 2048, 2049, 65]
+    rows = len(lengths)
+    case = cases.make_case(lengths, hq, hkv, d, seed=21, capacity=4096)
+    q, k, v, table, lens = device_case(case)
+    bits = ops.FLAG_BALANCED | {"dynamic+skip": ops.FLAG_DYNAMIC | ops.FLAG_SKIP_EMPTY}.get(flags, 0)
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
+    nan = dict(device="cuda", dtype=torch.float32)
+    out = torch.empty(rows, hq, d, dtype=torch.bfloat16, device="cuda")
+    if protocol == "lse":
+        ws = dict(partial=torch.full((rows, hq, splits, d), float("nan"), **nan),
+                  lse=torch.full((rows, hq, splits), float("nan"), **nan))
+    else:
+        ws = dict(maxima=torch.full((rows, hq, splits), float("nan"), **nan),
+                  denoms=torch.full((rows, hq, splits), float("nan"), **nan),
+                  accums=torch.full((rows, hq, splits, d), float("nan"), **nan))
+    args = ops.decode_args(q, k, v, table, lens, scale=0.09, tokens_per_split=granule,
+                           splits=splits,
+                           protocol=ops.PROTOCOL_LSE if protocol == "lse" else ops.PROTOCOL_MLA,
+                           kernel=kernel, flags=bits, out=out, counters=counters, **ws)
+    for _ in range(2):
+        ops.paged_decode(args, q.device)
+    torch.cuda.synchronize()
+    assert not counters.any() and ops.read_fault() == 0
+    assert_out_close(out, oracle.dense_reference(*case.arrays(), scale=0.09))
+    bounds = [oracle.partition_bounds(n, granule, splits, balanced=True) for n in lengths]
+    live = torch.tensor([[e > s for s, e in b] for b in bounds], device="cuda")
+    live = live[:, None, :].expand(rows, hq, splits)
+    m = live.cpu().numpy()
+    skip = bool(bits & ops.FLAG_SKIP_EMPTY)
+    mags = oracle.score_magnitudes(*case.arrays()[:2], case.table, case.lengths, granule, splits,
+                                   0.09, balanced=True)
+    if protocol == "lse":
+        ref_p, ref_l = oracle.normalized_partitions(*case.arrays(), granule, splits, scale=0.09,
+                                                    balanced=True)
+        assert_lse_close(ws["lse"][live], ref_l[m], score_mag=mags[m])
+        assert_out_close(ws["partial"][live], ref_p[m], "live partials")
+        empty_l, empty_p = ws["lse"][~live], ws["partial"][~live]
+        if skip:
+            assert torch.isnan(empty_l).all() and torch.isnan(empty_p).all()
+        else:
+            assert torch.isneginf(empty_l).all() and not empty_p.any()
+    else:
+        ref_m, ref_d, _ = oracle.unnormalized_partitions(*case.arrays(), granule, splits,
+                                                         scale=0.09, balanced=True)
+        assert_lse_close(ws["maxima"][live], ref_m[m], "maxima", score_mag=mags[m])
+        assert np.allclose(ws["denoms"][live].cpu().numpy(), ref_d[m], rtol=1e-5)
+        empty = [ws["maxima"][~live], ws["denoms"][~live], ws["accums"][~live]]
+        if skip:
+            assert all(torch.isnan(t).all() for t in empty)
+        else:
+            assert torch.isneginf(empty[0]).all() and not empty[1].any() and not empty[2].any()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_balanced_partitions_over_several_waves(kernel):
+    """More balanced items than CTA slots (dense enumeration, several waves):
+    static and dynamic scheduling give the same bits and the oracle's output."""
+    gen = np.random.default_rng(5)
+    lengths = gen.integers(0, 1500, size=300)
+    lengths[::9] = 0
+    case = cases.make_case(lengths, 8, 2, 128, seed=31, capacity=1536)
+    q, k, v, table, lens = device_case(case)
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = []
+    for flags in (ops.FLAG_BALANCED, ops.FLAG_BALANCED | ops.FLAG_DYNAMIC):
+        out = torch.empty(300, 8, 128, dtype=torch.bfloat16, device="cuda")
+        lse = torch.full((300, 8, 4), float("nan"), device="cuda")
+        partial = torch.full((300, 8, 4, 128), float("nan"), device="cuda")
+        args = ops.decode_args(q, k, v, table, lens, scale=0.09, tokens_per_split=64, splits=4,
+                               protocol=ops.PROTOCOL_LSE, kernel=kernel, flags=flags, out=out,
+                               partial=partial, lse=lse, counters=counters)
+        ops.paged_decode(args, q.device)
+        outs.append((out, lse))
+    torch.cuda.synchronize()
+    assert not counters.any() and ops.read_fault() == 0
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    few = list(range(0, 300, 23))
+    want = oracle.dense_reference(case.q[few], case.k, case.v, case.table[few], case.lengths[few],
+                                  scale=0.09)
+    assert_out_close(outs[1][0][few], want)

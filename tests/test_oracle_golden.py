@@ -122,6 +122,21 @@ def test_partition_bounds_integer_contract():
     assert oracle.partition_bounds(1024, 1024, 2) == [(0, 1024), (1024, 1024)]
 
 
+def test_balanced_partition_bounds_cover_each_row_in_equal_granule_multiples():
+    assert oracle.partition_bounds(2064, 64, 2, balanced=True) == [(0, 1088), (1088, 2064)]
+    assert oracle.partition_bounds(0, 64, 3, balanced=True) == [(0, 0)] * 3
+    for n in range(0, 3000, 37):
+        for splits in (1, 2, 3, 7, 40):
+            for granule in (32, 64, 128):
+                b = oracle.partition_bounds(n, granule, splits, balanced=True)
+                span = oracle.balanced_span(n, splits, granule)
+                assert span % granule == 0 and span * splits >= n
+                live = [(s, e) for s, e in b if e > s]
+                assert [s for s, _ in live] == [p * span for p in range(len(live))]
+                assert sum(e - s for s, e in live) == n
+                assert all(e - s == span for s, e in live[:-1])
+
+
 def test_all_empty_lse_merge_gives_zero():
     partials = np.zeros((1, 2, 3, 8), np.float32)
     lse = np.full((1, 2, 3), -np.inf, np.float32)
