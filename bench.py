@@ -322,13 +322,20 @@ def measured_peak():
     return 6650.0, "fallback 6.65 TB/s"
 
 
-def committed_traffic(workload, kernel):
-    """Per-launch DRAM bytes from the ncu summary committed under profiles/."""
+def committed_traffic(workload, kernel, kv_bytes):
+    """Per-launch DRAM bytes from the ncu summary committed under profiles/
+    (line ``traffic[workload][kernel]: BYTES of KV_BYTES``), scaled by the KV
+    bytes when this launch reads a different amount than the captured one."""
     for path in sorted((ROOT / "profiles").glob("*.md")):
-        m = re.search(rf"^traffic\[{re.escape(workload)}\]\[{re.escape(kernel)}\]:\s*(\d+)",
-                      path.read_text(), re.M)
+        m = re.search(rf"^traffic\[{re.escape(workload)}\]\[{re.escape(kernel)}\]:\s*(\d+)"
+                      rf"(?:\s+of\s+(\d+))?", path.read_text(), re.M)
         if m:
-            return int(m.group(1)), f"committed ncu summary profiles/{path.name}"
+            src = f"committed ncu summary profiles/{path.name}"
+            traffic, captured = int(m.group(1)), int(m.group(2) or 0)
+            if captured and captured != kv_bytes:
+                traffic = int(traffic * kv_bytes / captured)
+                src += f" (scaled from {captured} KV bytes)"
+            return traffic, src
     return None, None
 
 
@@ -727,7 +734,7 @@ def main(argv=None):
     group = gspec.num_heads // gspec.num_kv_heads
     kernel_name = "mma" if (args.kernel == "mma" or (args.kernel == "auto" and group >= 3)) \
         else "simt"
-    traffic, traffic_src = committed_traffic(args.config, kernel_name)
+    traffic, traffic_src = committed_traffic(args.config, kernel_name, glob.kv_bytes)
     if traffic is not None and strong:
         global_bytes = job_bytes
         traffic = int(traffic * local_bytes / max(global_bytes, 1))  # this rank's share
