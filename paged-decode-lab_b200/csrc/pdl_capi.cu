@@ -462,6 +462,14 @@ extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *pla
   // items 0.81, 384 items 0.78) and one wave stays.
   if (spec->head_dim <= 128 && groups * splits < 2 * slots && capacity / splits > 1024)
     splits = (2 * slots + groups - 1) / groups;
+  // At D = 256, between one and two waves of whole-row items the second wave
+  // leaves most CTAs idle; two balanced partitions per row (3.5 waves) keep
+  // them busy (config 3 B=128 per step: 173.6 -> 171.8 us at ctx 2064, the
+  // partition kernel 0.963 -> 0.992 of copy bandwidth; 54.7 -> 53.3 us at
+  // ctx 528.  B=64, one wave of rows, stays at 1: 86.5 vs 90.5 us).
+  const bool d256_rows_wave = spec->head_dim == 256 && splits == 1 && groups > slots &&
+                              groups < 2 * slots;
+  if (d256_rows_wave) splits = 2;
   splits = std::min<int64_t>(std::max<int64_t>(splits, 1), blocks);
   const int64_t tps = (blocks + splits - 1) / splits * tile;
   splits = (capacity + tps - 1) / tps;  // drop partitions that would always be empty
@@ -469,8 +477,8 @@ extern "C" int pdl_b200_plan(const PdlSpec *spec, int32_t sm_count, PdlPlan *pla
   // but rows are often shorter (config 3: 2064 of 2560 tokens splits into
   // 1280 + 784 with fixed bounds), so the plan recommends partitions that
   // follow each row's length (PDL_FLAG_BALANCED, granule tile_tokens).
-  const bool balanced = spec->head_dim == 256 && splits > 1 && groups * splits <= slots &&
-                        tps > 4 * tile;
+  const bool balanced = spec->head_dim == 256 && splits > 1 && tps > 4 * tile &&
+                        (groups * splits <= slots || d256_rows_wave);
   int64_t padded = 1;
   while (padded < splits) padded <<= 1;
   plan->splits = (int32_t)splits;

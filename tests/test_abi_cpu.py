@@ -161,9 +161,12 @@ def test_b200_plan_recommends_balanced_partitions_for_one_wave_of_long_d256_item
     plan = make_b200_plan(DecodeSpec(32, 16, 4, 256, 2320), 148)
     assert (plan.splits, plan.tokens_per_split, plan.balanced) == (2, 1280, True)
     assert launch_partitioning(plan) == (64, _lib.FLAG_BALANCED)
-    # B=1 (40 items of 64 tokens), one full wave of 2560 tokens, D = 128: fixed bounds.
-    for spec in (DecodeSpec(1, 16, 4, 256, 2320), DecodeSpec(128, 16, 4, 256, 2320),
-                 DecodeSpec(128, 32, 8, 128, 32768)):
+    # Between one and two waves of whole rows: two balanced partitions per row.
+    plan = make_b200_plan(DecodeSpec(128, 16, 4, 256, 2320), 148)
+    assert (plan.splits, plan.tokens_per_split, plan.balanced) == (2, 1280, True)
+    # B=1 (40 items of 64 tokens), one wave of whole rows, three waves, D = 128: fixed bounds.
+    for spec in (DecodeSpec(1, 16, 4, 256, 2320), DecodeSpec(64, 16, 4, 256, 2320),
+                 DecodeSpec(256, 16, 4, 256, 2320), DecodeSpec(128, 32, 8, 128, 32768)):
         plan = make_b200_plan(spec, 148)
         assert not plan.balanced and launch_partitioning(plan) == (plan.tokens_per_split, 0)
 
