@@ -308,7 +308,9 @@ typedef struct PdlExchangeArgs {
   const float *lse;           /* f32 [rows, parts]                                        */
   const int32_t *lengths;     /* optional int32 [rows / num_heads] tokens of each row in this
                                * rank's range: only ceil(len / tokens_per_split) partitions
-                               * are read; NULL reads all `parts`                         */
+                               * are read (fixed bounds: a workspace written with
+                               * PDL_FLAG_BALANCED needs lengths NULL); NULL reads all
+                               * `parts`                                                  */
   int32_t num_heads;
   int32_t tokens_per_split;
   int32_t rows;
