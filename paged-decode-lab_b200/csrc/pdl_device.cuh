@@ -131,8 +131,8 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 // balanced partitions of whole granules: granule * ceil(ceil(len / splits) /
 // granule); 0 for an empty row.  Partition p covers [p * span, (p + 1) *
 // span) of the row; the partition and merge kernels both use this.
-__host__ __device__ __forceinline__ int balanced_span(int len, int splits, int granule) {
-  const int per = (len + splits - 1) / splits;
+__host__ __device__ __forceinline__ int64_t balanced_span(int len, int splits, int granule) {
+  const int64_t per = ((int64_t)len + splits - 1) / splits;
   return (per + granule - 1) / granule * granule;
 }
 

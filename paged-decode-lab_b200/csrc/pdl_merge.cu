@@ -61,8 +61,8 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS)
     if (!p.early_lengths) len = __ldg(p.lengths + row / p.num_heads);
     if (p.balanced) {
       const int clamped = min(max(len, 0), p.cap_tokens);
-      const int span = balanced_span(clamped, p.splits, p.tokens_per_split);
-      live = span > 0 ? min(live, (clamped + span - 1) / span) : 0;
+      const int64_t span = balanced_span(clamped, p.splits, p.tokens_per_split);
+      live = span > 0 ? (int)min((int64_t)live, (clamped + span - 1) / span) : 0;
     } else {
       live = min(live, (int)((max(len, 0) + (int64_t)p.tokens_per_split - 1) / p.tokens_per_split));
     }
