@@ -268,10 +268,11 @@ static __device__ __noinline__ WorkItem decode_live(const SchedParams p, const L
   return w;
 }
 
-// Single-wave launches (at most one item per CTA) and batches above
-// 32 * RMAX rows enumerate every (row, KV head, sub-group, partition)
-// instead; empty ones become single-partition FILL items (or are skipped
-// when empty partitions are not stored).  The row length and the first 32
+// Single-wave launches (at most one item per CTA), batches above 32 * RMAX
+// rows and balanced partition bounds (derived per item from the row's
+// length) enumerate every (row, KV head, sub-group, partition) instead;
+// empty ones become single-partition FILL items (or are skipped when empty
+// partitions are not stored).  The row length and the first 32
 // block-table entries of the partition are requested together, so an item,
 // and its first pages, are known after one round trip.
 //   static:  item = ((b * num_kv_heads + kvh) * nsub + sub) * splits + split
