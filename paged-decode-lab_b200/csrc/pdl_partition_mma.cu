@@ -404,9 +404,9 @@ __global__ void __launch_bounds__(MmaShape<D>::NTHREADS, 2)
         }
       }
     }
-    ring_peek(ring, ik, cw == 0 && lane == 0);
+    if (!w.last) ring_peek(ring, ik, cw == 0 && lane == 0);
     named_barrier(1, NC * 32);
-    {
+    if (!w.last) {  // a CTA's last item has no next one to prepare
       // The next item's q rows into L1 while this one is combined (each of a
       // row's D/64 lines by one of the four lanes that load it).
       const WorkItem nx = peeked_item(ring, ik);

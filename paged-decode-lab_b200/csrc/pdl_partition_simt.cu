@@ -248,9 +248,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         comb_ml[cw * 2 * GC + GC + g] = l[g];
       }
     }
-    ring_peek(ring, ik, cw == 0 && lane == 0);
+    if (!w.last) ring_peek(ring, ik, cw == 0 && lane == 0);
     named_barrier(1, NC * 32);
-    {
+    if (!w.last) {  // a CTA's last item has no next one to prepare
       // The next item's q chunks into L1 while this one is combined.
       const WorkItem nx = peeked_item(ring, ik);
       if (nx.kind == ITEM_COMPUTE) {
