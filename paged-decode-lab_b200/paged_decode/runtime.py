@@ -5,11 +5,13 @@ Drop-in for the reference's ``src/paged_decode/runtime.py``: the same
 ``validate_device_metadata`` surface, backend names and ``ValueError``
 messages, with every backend served by the sm_100a kernels of this package:
 
-  triton_base       single pass per row (CUDA-core kernel, tensor cores from 3
-                    query heads per KV head)
+  triton_base       one output per row, no exposed workspace (CUDA-core kernel,
+                    tensor cores from 3 query heads per KV head); rows longer
+                    than this library's plan allows per CTA are split into
+                    internal scratch and merged (see allocate_resources)
   triton_splitk     1024-token partitions, (m, l, acc) workspace + merge (kernel
                     chosen as for triton_base)
-  triton_tc         single pass per row, BF16 tensor-core kernel
+  triton_tc         as triton_base, BF16 tensor-core kernel
   triton_tc_splitk  1024-token partitions, (m, l, acc) workspace + merge, tensor cores
 
 Tensor CONTENTS are trusted on the hot path (live table entries must be valid
@@ -37,8 +39,13 @@ class Resources:
     denoms: torch.Tensor | None = None
     accums: torch.Tensor | None = None
     # The two scheduler words of the dynamically scheduled partition kernel;
-    # zeroed, split backends only, left zeroed by the kernels.
+    # zeroed, left zeroed by the kernels.
     counters: torch.Tensor | None = None
+    # Not in the reference: the single-pass backends' split plan and scratch
+    # (partial + LSE per partition), or None where one pass per row is used.
+    split_plan: object | None = None
+    split_partials: torch.Tensor | None = None
+    split_lse: torch.Tensor | None = None
 
 
 def allocate_resources(spec, device, backend="triton_splitk"):
@@ -46,6 +53,10 @@ def allocate_resources(spec, device, backend="triton_splitk"):
 
     Shapes follow the reference (runtime.py:24-35): out bf16 [B,Hq,D];
     maxima / denoms f32 [B,Hq,partitions]; accums f32 [B,Hq,partitions,D].
+    The single-pass backends additionally get this library's split plan for
+    the device and, when it splits rows, partial + LSE scratch for it: one
+    CTA per (row, KV head) leaves most of a B200 idle or streams a long row
+    alone (config 4: 634 us in one pass against 459 us split).
     """
     if backend not in _CUSTOM:
         raise ValueError("resources require a custom backend")
@@ -58,6 +69,16 @@ def allocate_resources(spec, device, backend="triton_splitk"):
         result.denoms = torch.empty(shape, device=device, dtype=torch.float32)
         result.accums = torch.empty((*shape, spec.head_dim), device=device, dtype=torch.float32)
         result.counters = torch.zeros(2, device=device, dtype=torch.int32)
+    elif torch.device(device).type == "cuda":
+        from .splitkv_plan import make_b200_plan
+        plan = make_b200_plan(spec, ops.sm_count(device))
+        if plan.splits > 1:
+            shape = (spec.max_batch, spec.num_heads, plan.splits)
+            result.split_plan = plan
+            result.split_partials = torch.empty((*shape, spec.head_dim), device=device,
+                                                dtype=torch.float32)
+            result.split_lse = torch.empty(shape, device=device, dtype=torch.float32)
+            result.counters = torch.zeros(2, device=device, dtype=torch.int32)
     return result
 
 
@@ -142,7 +163,7 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
     cache = resources.__dict__.setdefault("_launches", ops.LaunchCache())
     key = ((backend, scale, q.device) + ops.tensor_key(q, k, v, tables, lengths)
            + ops.buffers_key(resources.out, resources.maxima, resources.denoms, resources.accums,
-                             resources.counters))
+                             resources.counters, resources.split_partials))
     args = cache.get(key)
     if args is not None:
         ops.paged_decode(args, q.device)
@@ -184,6 +205,18 @@ def paged_decode(q, k, v, tables, lengths, *, resources, backend="triton_base", 
                                maxima=resources.maxima, denoms=resources.denoms,
                                accums=resources.accums, counters=resources.counters,
                                flags=flags)
+    elif resources.split_plan is not None:
+        # One output per row, computed in partitions of this library's plan
+        # (scratch only: partitions past a row's length are not stored).
+        from .splitkv_plan import launch_partitioning
+        plan = resources.split_plan
+        tokens, bounds = launch_partitioning(plan)
+        args = ops.decode_args(q, k, v, tables, lengths, scale=scale,
+                               tokens_per_split=tokens, splits=plan.splits,
+                               protocol=ops.PROTOCOL_LSE, kernel=kernel, out=resources.out,
+                               partial=resources.split_partials, lse=resources.split_lse,
+                               counters=resources.counters,
+                               flags=bounds | ops.FLAG_SKIP_EMPTY | ops.FLAG_DYNAMIC)
     else:
         args = ops.decode_args(q, k, v, tables, lengths, scale=scale, kernel=kernel,
                                out=resources.out)
