@@ -160,3 +160,31 @@ def test_config1_all_backends_against_golden(golden):
         assert_out_close(out, golden["cfg1/dense"], backend)
         assert_out_close(out, golden["cfg1/split"], backend)
         assert torch.count_nonzero(out[0]) == 0
+
+
+@pytest.mark.parametrize("backend", ["triton_base", "triton_tc"])
+@pytest.mark.parametrize("spec_args,lengths", [
+    ((8, 16, 4, 256, 2320), [2064, 528, 0, 1, 2320, 1031, 64, 700]),     # balanced partitions
+    ((6, 8, 2, 128, 9000), [9000, 0, 4096, 4097, 17, 8191]),            # fixed partitions
+])
+def test_single_pass_backends_split_like_the_b200_plan(backend, spec_args, lengths):
+    """The single-pass backends compute rows in this library's plan (internal
+    scratch, empty partitions not stored) when it has more than one partition:
+    the output is the one of matched_decode with that plan, bit for bit, and
+    within the output tolerance of the dense softmax."""
+    from paged_decode import ops
+    from paged_decode.matched_splitkv import allocate_matched_resources, matched_decode
+    from paged_decode.splitkv_plan import make_b200_plan
+    spec = DecodeSpec(*spec_args)
+    case = cases.make_case(lengths, spec.num_heads, spec.num_kv_heads, spec.head_dim, seed=41,
+                           capacity=spec.max_context_len)
+    args = device_case(case)
+    res = allocate_resources(spec, "cuda", backend)
+    assert res.split_plan is not None and res.split_plan.splits > 1
+    out = paged_decode(*args, resources=res, backend=backend).clone()
+    plan = make_b200_plan(spec, ops.sm_count(torch.device("cuda")))
+    mres = allocate_matched_resources(spec, "cuda", plan=plan)
+    want = matched_decode(*args, resources=mres, kernel="mma" if backend == "triton_tc" else "auto")
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert_out_close(out, oracle.dense_reference(*case.arrays()))
