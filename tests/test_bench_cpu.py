@@ -64,3 +64,17 @@ def test_default_workload_and_modes():
     assert bench.resolve_mode(bench.parse_args(["--config", "cfg5"]), 4) == "context"
     assert bench.resolve_mode(bench.parse_args(["--mode", "head"]), 2) == "head"
     assert bench.resolve_mode(bench.parse_args(["--mode", "replica"]), 2) == "replica"
+
+
+def test_committed_traffic_is_scaled_to_the_launch_kv_bytes():
+    """The per-launch DRAM bytes come from the ncu summaries under profiles/
+    (``traffic[config][kernel]: BYTES of KV_BYTES``) and are scaled by the KV
+    bytes of the launch the bench measured."""
+    sys.path.insert(0, str(ROOT))
+    import importlib
+    bench = importlib.import_module("bench")
+    traffic, src = bench.committed_traffic("cfg4", "mma", 3074609152)
+    assert traffic == 3119899360 and "profiles/" in src and "scaled" not in src
+    half, src = bench.committed_traffic("cfg4", "mma", 3074609152 // 2)
+    assert abs(half - 3119899360 // 2) <= 1 and "scaled" in src
+    assert bench.committed_traffic("cfg1", "mma", 1) == (None, None)
